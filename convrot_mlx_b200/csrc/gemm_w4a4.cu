@@ -1,0 +1,508 @@
+// W4A4 GEMM for sm_100a: int8 activation codes x packed signed-int4 weights on
+// tcgen05 (kind::i8), int32 accumulators in TMEM, fused scale/bias epilogue.
+//
+// Replaces the reference's MPP TensorOp dot (core.py:839-874) plus its
+// separate int32 -> scale/bias epilogue dispatch (core.py:925-937, 994-1011):
+// here the int32 dots never leave the SM.
+//
+// Persistent kernel, one CTA per SM, tile 128 (M) x 256 (N) x 128 (K bytes):
+//   warp 0      TMA producer: int8 activation tiles, 128-byte swizzle
+//   warp 1      MMA issuer (one elected thread) + TMEM owner
+//   warps 2-9   weight transform: 16-byte global loads of packed nibbles,
+//               expanded to int8 in the canonical 128-byte-swizzled layout the
+//               tensor core reads (K-major for the NK layout, MN-major for KN)
+//   warps 10-13 epilogue: TMEM -> registers -> out = T(f32(dot) * xs * ws + b)
+// Weight nibbles are expanded as 16 * w (the nibble moved to the high half of
+// the byte: one AND, no sign extension), so the accumulator holds 16 * dot
+// exactly; the epilogue shifts it back (|dot| <= 56 K stays far below 2^27).
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
+// the main loop of tile i + 1.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace convrot {
+
+__device__ int g_convrot_device_error = 0;
+
+namespace w4a4 {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes of K per stage
+constexpr int STAGES = 4;
+constexpr int kWarpTma = 0;
+constexpr int kWarpMma = 1;
+constexpr int kWarpXform0 = 2;
+constexpr int kXformWarps = 8;
+constexpr int kWarpEpi0 = kWarpXform0 + kXformWarps;
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = (kWarpEpi0 + kEpiWarps) * 32;  // 448
+constexpr int kXformThreads = kXformWarps * 32;
+constexpr int kItems = BN * BK / 32;  // 16 packed bytes -> 32 int8 per item
+constexpr int kItemsPerThread = kItems / kXformThreads;  // 4
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr int kABytes = BM * BK;  // 16 KB
+constexpr int kBBytes = BN * BK;  // 32 KB
+constexpr uint64_t kTimeoutNs = 4000000000ull;  // a single wait never legitimately takes this long
+
+struct alignas(8) Barriers {
+  uint64_t a_full[STAGES];
+  uint64_t b_full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int err;
+};
+
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBBytes) + sizeof(Barriers);
+
+struct Params {
+  const uint8_t* qweight;
+  const float* xscales;
+  const float* wscales;
+  const float* bias;
+  void* out;
+  int M, N, K;
+  int m_tiles, n_tiles, k_blocks;
+  int layout;
+};
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase of `bar` with parity `parity` to complete, for at most
+// kTimeoutNs.  On time-out record the error in shared memory and return false.
+__device__ __noinline__ bool wait_bar(uint64_t* bar, uint32_t parity, Barriers* b, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*reinterpret_cast<volatile int*>(&b->err)) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        atomicCAS(&b->err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// 16 packed bytes -> 32 int8 values of 16 * nibble, in element order.
+__device__ __forceinline__ void expand16(const uint4 w, uint32_t (&o)[8]) {
+  const uint32_t s[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t even = (s[j] << 4) & 0xF0F0F0F0u;  // elements 0,2,4,6 of this word
+    const uint32_t odd = s[j] & 0xF0F0F0F0u;          // elements 1,3,5,7
+    o[2 * j] = __byte_perm(even, odd, 0x5140);
+    o[2 * j + 1] = __byte_perm(even, odd, 0x7362);
+  }
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Location of transform item `item` of a stage: global byte offset (or -1 when
+// it lies outside the weight) and the two smem chunk offsets of its 32 bytes.
+template <int LAYOUT>
+__device__ __forceinline__ void item_geometry(const Params& p, int item, int n0, int k0, int64_t& goff, bool& vec_ok,
+                                              uint32_t& s0, uint32_t& s1) {
+  if constexpr (LAYOUT == CONVROT_LAYOUT_NK) {
+    const int n = item >> 2, q = item & 3;
+    const int gn = n0 + n, gk = k0 + 32 * q;
+    goff = (gn < p.N && gk < p.K) ? static_cast<int64_t>(gn) * (p.K >> 1) + (gk >> 1) : -1;
+    vec_ok = true;
+    const uint32_t row = (n >> 3) * 1024 + (n & 7) * 128;
+    s0 = row + (((2 * q) ^ (n & 7)) << 4);
+    s1 = row + (((2 * q + 1) ^ (n & 7)) << 4);
+  } else {
+    const int wi = item >> 5, lane = item & 31;
+    const int kr = 4 * wi + ((lane >> 2) & 3);
+    const int q = (lane & 3) + 4 * (lane >> 4);
+    const int gk = k0 + kr, gn = n0 + 32 * q;
+    goff = (gk < p.K && gn < p.N) ? static_cast<int64_t>(gk) * (p.N >> 1) + (gn >> 1) : -1;
+    vec_ok = ((p.N & 31) == 0) || (gn + 32 <= p.N);
+    const uint32_t base = (q >> 2) * (BK * 128) + (kr >> 3) * 1024 + (kr & 7) * 128;
+    const int c = 2 * (q & 3);
+    s0 = base + ((c ^ (kr & 7)) << 4);
+    s1 = base + (((c + 1) ^ (kr & 7)) << 4);
+  }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ uint4 load_item(const Params& p, int64_t goff, bool vec_ok, int gn_base) {
+  if (goff < 0) return make_uint4(0, 0, 0, 0);
+  const uint8_t* src = p.qweight + goff;
+  if (LAYOUT == CONVROT_LAYOUT_NK || vec_ok) return __ldg(reinterpret_cast<const uint4*>(src));
+  // KN item crossing the N edge (N % 32 != 0): bytes one by one, zero past N.
+  uint32_t w[4] = {0, 0, 0, 0};
+  for (int b = 0; b < 16; ++b) {
+    if (gn_base + 2 * b < p.N) w[b >> 2] |= static_cast<uint32_t>(src[b]) << (8 * (b & 3));
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ int item_gn(int item, int n0) {
+  if constexpr (LAYOUT == CONVROT_LAYOUT_NK) {
+    return n0;
+  } else {
+    const int lane = item & 31;
+    return n0 + 32 * ((lane & 3) + 4 * (lane >> 4));
+  }
+}
+
+// 16 consecutive outputs with 16-byte stores (pointer 16-byte aligned).
+__device__ __forceinline__ void store16(float* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+template <typename T16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  const T16 lo = cvt_out<T16>(a), hi = cvt_out<T16>(b);
+  return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
+         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+}
+
+template <typename T16>
+__device__ __forceinline__ void store16(T16* dst, const float (&v)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+    reinterpret_cast<uint4*>(dst)[q] = make_uint4(pack2<T16>(v[8 * q], v[8 * q + 1]), pack2<T16>(v[8 * q + 2], v[8 * q + 3]),
+                                                  pack2<T16>(v[8 * q + 4], v[8 * q + 5]), pack2<T16>(v[8 * q + 6], v[8 * q + 7]));
+}
+
+template <int LAYOUT, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * kABytes;
+  Barriers* bars = reinterpret_cast<Barriers*>(sB + STAGES * kBBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bars->a_full[s], 1);
+      mbar_init(&bars->b_full[s], kXformWarps);
+      mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], kEpiWarps);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->err = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap_a);
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc(&bars->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == kWarpTma) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[STAGES];
+      uint32_t issued_phase[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile % p.m_tiles;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&bars->empty[stage], phase ^ 1, bars, 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->a_full[stage], kABytes);
+          tma_load_2d(sA + stage * kABytes, &tmap_a, &bars->a_full[stage], kb * BK, m_blk * BM);
+          issued[stage] = 1;
+          issued_phase[stage] = phase;
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // error exit: let the copies already in flight land before the CTA ends
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) wait_bar(&bars->a_full[s], issued_phase[s], bars, 1);
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (lane == 0) {
+      // idesc: D s32 (bits 4-5 = 2), A s8 (bits 7-9 = 1), B s8 (bits 10-12 = 1),
+      // A K-major, B K-major (NK) or MN-major (KN), N >> 3 at bit 17, M >> 4 at bit 24.
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                             (static_cast<uint32_t>(LAYOUT == CONVROT_LAYOUT_KN) << 16) |
+                             (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!wait_bar(&bars->acc_empty[buf], acc_phase ^ 1, bars, 2)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&bars->a_full[stage], phase, bars, 3)) { ok = false; break; }
+          if (!wait_bar(&bars->b_full[stage], phase, bars, 4)) { ok = false; break; }
+          tc_fence_after();
+          const int k_rem = p.K - kb * BK;
+          const int ksteps = k_rem >= BK ? BK / 32 : k_rem / 32;
+          const uint32_t a_addr = a_base + stage * kABytes;
+          const uint32_t b_addr = b_base + stage * kBBytes;
+          for (int ks = 0; ks < ksteps; ++ks) {
+            const uint64_t adesc = smem_desc(a_addr + ks * 32, 16, 1024, 2);
+            const uint64_t bdesc = LAYOUT == CONVROT_LAYOUT_NK ? smem_desc(b_addr + ks * 32, 16, 1024, 2)
+                                                               : smem_desc(b_addr + ks * 4096, BK * 128, 1024, 2);
+            mma_i8(d_tmem, adesc, bdesc, idesc, (kb | ks) != 0 ? 1u : 0u);
+          }
+          mma_commit(&bars->empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(&bars->acc_full[buf]);
+      }
+      // every MMA issued above must finish before TMEM is released
+      mma_commit(&bars->mma_done);
+      wait_bar(&bars->mma_done, 0, bars, 5);
+    }
+  } else if (warp < kWarpEpi0) {
+    // ---------------- weight transform ----------------
+    const int xt = threadIdx.x - kWarpXform0 * 32;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    uint4 cur[kItemsPerThread], nxt[kItemsPerThread];
+    int64_t goff[kItemsPerThread];
+    bool vec_ok[kItemsPerThread];
+    uint32_t s0[kItemsPerThread], s1[kItemsPerThread];
+    // block sequence of this CTA: (tile, kb) pairs; prefetch one block ahead
+    int tile = blockIdx.x, kb = 0;
+    auto issue = [&](int t, int k, uint4 (&dst)[kItemsPerThread]) {
+      const int n0 = (t / p.m_tiles) * BN;
+#pragma unroll
+      for (int i = 0; i < kItemsPerThread; ++i) {
+        const int item = i * kXformThreads + xt;
+        int64_t g;
+        bool v;
+        uint32_t a0, a1;
+        item_geometry<LAYOUT>(p, item, n0, k * BK, g, v, a0, a1);
+        dst[i] = load_item<LAYOUT>(p, g, v, item_gn<LAYOUT>(item, n0));
+      }
+    };
+    if (tile < num_tiles) issue(tile, 0, cur);
+    while (tile < num_tiles && ok) {
+      int ntile = tile, nkb = kb + 1;
+      if (nkb == p.k_blocks) { nkb = 0; ntile += gridDim.x; }
+      if (ntile < num_tiles) issue(ntile, nkb, nxt);
+      const int n0 = (tile / p.m_tiles) * BN;
+#pragma unroll
+      for (int i = 0; i < kItemsPerThread; ++i) {
+        const int item = i * kXformThreads + xt;
+        item_geometry<LAYOUT>(p, item, n0, kb * BK, goff[i], vec_ok[i], s0[i], s1[i]);
+      }
+      if (!wait_bar(&bars->empty[stage], phase ^ 1, bars, 6)) { ok = false; break; }
+      const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
+#pragma unroll
+      for (int i = 0; i < kItemsPerThread; ++i) {
+        uint32_t o[8];
+        expand16(cur[i], o);
+        sts128(b_addr + s0[i], o[0], o[1], o[2], o[3]);
+        sts128(b_addr + s1[i], o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->b_full[stage]);
+      if (++stage == STAGES) { stage = 0; phase ^= 1; }
+#pragma unroll
+      for (int i = 0; i < kItemsPerThread; ++i) cur[i] = nxt[i];
+      tile = ntile;
+      kb = nkb;
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      if (!wait_bar(&bars->acc_full[buf], acc_phase, bars, 7)) { ok = false; break; }
+      tc_fence_after();
+      const int m = m_blk * BM + ew * 32 + lane;
+      const bool row_ok = m < p.M;
+      const float xs = row_ok ? __ldg(p.xscales + m) : 0.0f;
+      TOut* orow = static_cast<TOut*>(p.out) + static_cast<int64_t>(row_ok ? m : 0) * p.N;
+      const bool vec_store = (p.N % (16 / sizeof(TOut))) == 0;
+      for (int c = 0; c < BN / 16; ++c) {
+        const int n = n_blk * BN + c * 16;
+        uint32_t r[16];
+        __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
+        tmem_ld_32x32b_x16(tmem_base + ((ew * 32u) << 16) + buf * BN + c * 16, r);
+        tmem_ld_wait();
+        if (n >= p.N) continue;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int col = min(n + j, p.N - 1);
+          const float ws = __ldg(p.wscales + col);
+          const float bb = p.bias ? __ldg(p.bias + col) : 0.0f;
+          const float dot = static_cast<float>(static_cast<int32_t>(r[j]) >> 4);
+          v[j] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), ws), bb);
+        }
+        if (!row_ok) continue;
+        if (vec_store && n + 16 <= p.N) {
+          store16(orow + n, v);
+        } else {
+          for (int j = 0; j < 16 && n + j < p.N; ++j) orow[n + j] = cvt_out<TOut>(v[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->acc_empty[buf]);
+    }
+  }
+
+  __syncwarp();  // roles above ran on single lanes: reconverge before the block barrier
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarpMma) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && bars->err) atomicCAS(&g_convrot_device_error, 0, bars->err);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                    uint32_t box_inner, uint32_t box_outer) {
+  auto encode = get_encode_fn();
+  CONVROT_REQUIRE(encode != nullptr, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem_strides[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CONVROT_REQUIRE(r == CUDA_SUCCESS, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return CONVROT_OK;
+}
+
+template <int LAYOUT, typename TOut>
+static int launch(const CUtensorMap& map, const Params& p, cudaStream_t stream) {
+  auto kernel = w4a4_gemm_kernel<LAYOUT, TOut>;
+  CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes)));
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < device_sm_count() ? tiles : device_sm_count();
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(map, p);
+  return check_launch("w4a4 gemm");
+}
+
+}  // namespace w4a4
+}  // namespace convrot
+
+extern "C" {
+
+int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
+                      const float* wscales, const float* bias, void* out, int out_dtype, int64_t m, int64_t n,
+                      int64_t k, void* stream) {
+  using namespace convrot;
+  CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || layout == CONVROT_LAYOUT_KN, CONVROT_ERR_INVALID, "unknown layout %d",
+                  layout);
+  CONVROT_REQUIRE(valid_dtype(out_dtype), CONVROT_ERR_INVALID, "unknown output dtype %d", out_dtype);
+  CONVROT_REQUIRE(m >= 0 && n > 0 && k > 0, CONVROT_ERR_INVALID, "invalid shape m=%lld n=%lld k=%lld",
+                  static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  CONVROT_REQUIRE(k % 32 == 0, CONVROT_ERR_INVALID, "W4A4 GEMM requires K divisible by 32, got %lld",
+                  static_cast<long long>(k));
+  CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || n % 2 == 0, CONVROT_ERR_INVALID,
+                  "K x packed-N weights require even N, got %lld", static_cast<long long>(n));
+  CONVROT_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CONVROT_ERR_UNSUPPORTED, "shape too large");
+  if (m == 0) return CONVROT_OK;
+  CONVROT_REQUIRE(act && qweight && xscales && wscales && out, CONVROT_ERR_INVALID, "null pointer");
+  CONVROT_REQUIRE(aligned_to(act, 16) && aligned_to(qweight, 16) && aligned_to(out, 16), CONVROT_ERR_INVALID,
+                  "activation, weight and output must be 16-byte aligned");
+  w4a4::Params p;
+  p.qweight = qweight;
+  p.xscales = xscales;
+  p.wscales = wscales;
+  p.bias = bias;
+  p.out = out;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.m_tiles = static_cast<int>((m + w4a4::BM - 1) / w4a4::BM);
+  p.n_tiles = static_cast<int>((n + w4a4::BN - 1) / w4a4::BN);
+  p.k_blocks = static_cast<int>((k + w4a4::BK - 1) / w4a4::BK);
+  CONVROT_REQUIRE(static_cast<int64_t>(p.m_tiles) * p.n_tiles < (1LL << 31), CONVROT_ERR_UNSUPPORTED,
+                  "too many output tiles");
+  p.layout = layout;
+  CUtensorMap map;
+  int rc = w4a4::make_tmap_2d_u8(&map, act, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
+                                 static_cast<uint64_t>(k), w4a4::BK, w4a4::BM);
+  if (rc != CONVROT_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (layout == CONVROT_LAYOUT_NK) {
+    switch (out_dtype) {
+      case CONVROT_BF16: return w4a4::launch<CONVROT_LAYOUT_NK, __nv_bfloat16>(map, p, s);
+      case CONVROT_F16: return w4a4::launch<CONVROT_LAYOUT_NK, __half>(map, p, s);
+      default: return w4a4::launch<CONVROT_LAYOUT_NK, float>(map, p, s);
+    }
+  }
+  switch (out_dtype) {
+    case CONVROT_BF16: return w4a4::launch<CONVROT_LAYOUT_KN, __nv_bfloat16>(map, p, s);
+    case CONVROT_F16: return w4a4::launch<CONVROT_LAYOUT_KN, __half>(map, p, s);
+    default: return w4a4::launch<CONVROT_LAYOUT_KN, float>(map, p, s);
+  }
+}
+
+// Read and clear the device-side error word set by a kernel whose bounded
+// wait timed out (0 = none).  Synchronizes the device.
+int convrot_take_device_error(int* code) {
+  int v = 0, zero = 0;
+  CONVROT_CUDA_CHECK(cudaDeviceSynchronize());
+  CONVROT_CUDA_CHECK(cudaMemcpyFromSymbol(&v, convrot::g_convrot_device_error, sizeof(int)));
+  CONVROT_CUDA_CHECK(cudaMemcpyToSymbol(convrot::g_convrot_device_error, &zero, sizeof(int)));
+  if (code) *code = v;
+  return CONVROT_OK;
+}
+
+}  // extern "C"

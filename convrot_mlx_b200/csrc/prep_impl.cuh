@@ -1,0 +1,390 @@
+// Fused ConvRot activation preparation for sm_100a.
+//
+// One CTA owns one row.  The row is read from HBM exactly once (the reference
+// Metal kernel, core.py:205-304, reads it twice: once for the absmax pass and
+// once to re-rotate and quantize).  The rotated row waits in shared memory
+// for the row absmax, then is quantized and written with 16-byte stores.
+//
+// Pair-words.  Element e of the first half of the row is paired with element
+// e + half (half = ceil(groups / 2) * G), which sits at the same position of
+// another Hadamard group.  No butterfly stage ever mixes the two, so every
+// stage runs on packed bf16x2 / half2 words (two rows of the butterfly per
+// instruction).  A thread works on "units" of 16 consecutive pair-words:
+//   phase 1  global -> registers, butterfly strides 1 and 4 in registers
+//   phase 2  (G >= 64) strides 16 and 64 over columns of shared memory
+//   phase 3  (G == 1024) stride 256
+//   quantize rotated pair-words -> codes, one 16-byte store per half-unit.
+// Every add/sub is rounded to the input dtype in the reference's order
+// (core.py:180-201: ((a+b)+c)-d, ((a+b)-c)+d, ((a-b)+c)+d, ((-a+b)+c)+d),
+// then x / sqrt(G) (exact), scale = T(T(max(absmax, T(1e-10))) / 7) and
+// code = clamp(rint(T(x / scale)), -7, 7) (core.py:149-158, :258-298).
+#pragma once
+#include "common.cuh"
+
+namespace convrot {
+
+enum PrepMode : int { kModeI8 = 0, kModePacked = 1, kModeRotate = 2 };
+
+// Word index of pair-element p in shared memory: rows of 32 words, 16-byte
+// chunks XOR-swizzled so that the row-wise (phase 1 / quantize) and the
+// column-wise (phases 2 and 3) accesses are all free of bank conflicts.
+__device__ __forceinline__ int swz(int p) {
+  const int r = p >> 5;
+  const int h = (r & 3) | ((((r >> 1) ^ (r >> 3)) & 1) << 2);
+  return (r << 5) | ((((p >> 2) & 7) ^ h) << 2) | (p & 3);
+}
+
+template <typename E, typename P>
+__device__ __forceinline__ void bfly4(P& a, P& b, P& c, P& d) {
+  const P s = E::add(a, b);
+  const P t = E::sub(a, b);
+  const P u = E::sub(b, a);  // == (-a) + b, including the sign of zero
+  const P o0 = E::sub(E::add(s, c), d);
+  const P o1 = E::add(E::sub(s, c), d);
+  const P o2 = E::add(E::add(t, c), d);
+  const P o3 = E::add(E::add(u, c), d);
+  a = o0;
+  b = o1;
+  c = o2;
+  d = o3;
+}
+
+template <typename P>
+__device__ __forceinline__ void st_chunk(P* sm, int p, const P& v0, const P& v1, const P& v2, const P& v3) {
+  P* dst = sm + swz(p);
+  if constexpr (sizeof(P) == 4) {
+    uint4 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&v0);
+    u.y = *reinterpret_cast<const uint32_t*>(&v1);
+    u.z = *reinterpret_cast<const uint32_t*>(&v2);
+    u.w = *reinterpret_cast<const uint32_t*>(&v3);
+    *reinterpret_cast<uint4*>(dst) = u;
+  } else {
+    dst[0] = v0;
+    dst[1] = v1;
+    dst[2] = v2;
+    dst[3] = v3;
+  }
+}
+
+template <typename P>
+__device__ __forceinline__ void ld_chunk(const P* sm, int p, P& v0, P& v1, P& v2, P& v3) {
+  const P* src = sm + swz(p);
+  if constexpr (sizeof(P) == 4) {
+    const uint4 u = *reinterpret_cast<const uint4*>(src);
+    v0 = *reinterpret_cast<const P*>(&u.x);
+    v1 = *reinterpret_cast<const P*>(&u.y);
+    v2 = *reinterpret_cast<const P*>(&u.z);
+    v3 = *reinterpret_cast<const P*>(&u.w);
+  } else {
+    v0 = src[0];
+    v1 = src[1];
+    v2 = src[2];
+    v3 = src[3];
+  }
+}
+
+// Raw 16-element half-units as loaded from global memory.
+template <typename T> struct Raw16 {
+  static constexpr int kVec = 16 * sizeof(T) / 16;  // uint4 per 16 elements
+  uint4 v[kVec];
+};
+
+template <typename T>
+__device__ __forceinline__ void load16(Raw16<T>& r, const T* src) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < Raw16<T>::kVec; ++i) r.v[i] = __ldg(s + i);
+}
+
+template <typename T>
+__device__ __forceinline__ void zero16(Raw16<T>& r) {
+#pragma unroll
+  for (int i = 0; i < Raw16<T>::kVec; ++i) r.v[i] = make_uint4(0, 0, 0, 0);
+}
+
+template <typename T>
+__device__ __forceinline__ T raw_elem(const Raw16<T>& r, int i) {
+  return reinterpret_cast<const T*>(r.v)[i];
+}
+
+template <typename E, typename T, typename P>
+__device__ __forceinline__ void interleave(P (&v)[16], const Raw16<T>& lo, const Raw16<T>& hi) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = E::make(raw_elem(lo, i), raw_elem(hi, i));
+}
+
+// Radix-4 stages with strides 1 and 4 over 16 registers (stride 1 only for G == 4).
+template <typename E, int G, typename P>
+__device__ __forceinline__ void stages_1_4(P (&v)[16]) {
+  if constexpr (G >= 4) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly4<E>(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  }
+  if constexpr (G >= 16) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bfly4<E>(v[j], v[j + 4], v[j + 8], v[j + 12]);
+  }
+}
+
+template <typename E, typename P>
+__device__ __forceinline__ float normalize_absmax(P (&v)[16], P nrm, float amax) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = E::mul(v[i], nrm);
+    amax = fmaxf(amax, fmaxf(fabsf(E::to_f(E::lo(v[i]))), fabsf(E::to_f(E::hi(v[i])))));
+  }
+  return amax;
+}
+
+template <typename E, typename T>
+__device__ __forceinline__ int code_of(T v, float scale) {
+  const float ratio = E::to_f(E::from_f(__fdiv_rn(E::to_f(v), scale)));
+  const int q = __float2int_rn(ratio);  // half to even; NaN -> 0
+  return min(max(q, -7), 7);
+}
+
+// Write 16 outputs of one half-unit.
+template <typename E, typename T, int MODE>
+__device__ __forceinline__ void write_half(void* out, int64_t row, int64_t K, int64_t col, const T (&e)[16],
+                                           float scale) {
+  if constexpr (MODE == kModeI8) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint32_t acc = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc |= (static_cast<uint32_t>(code_of<E>(e[4 * j + b], scale)) & 0xFFu) << (8 * b);
+      w[j] = acc;
+    }
+    int8_t* o = static_cast<int8_t*>(out) + row * K + col;
+    *reinterpret_cast<uint4*>(o) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else if constexpr (MODE == kModePacked) {
+    uint32_t w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      uint32_t acc = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) acc |= (static_cast<uint32_t>(code_of<E>(e[8 * j + b], scale)) & 0xFu) << (4 * b);
+      w[j] = acc;
+    }
+    uint8_t* o = static_cast<uint8_t*>(out) + row * (K / 2) + col / 2;
+    *reinterpret_cast<uint2*>(o) = make_uint2(w[0], w[1]);
+  } else {
+    T* o = static_cast<T*>(out) + row * K + col;
+    const uint4* s = reinterpret_cast<const uint4*>(e);
+    uint4* d = reinterpret_cast<uint4*>(o);
+#pragma unroll
+    for (int i = 0; i < Raw16<T>::kVec; ++i) d[i] = s[i];
+  }
+}
+
+template <typename E, typename T, int MODE, typename P>
+__device__ __forceinline__ void emit_unit(void* out, int64_t row, int64_t K, int half, int p0, const P (&v)[16],
+                                          float scale) {
+  T lo[16], hi[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    lo[i] = E::lo(v[i]);
+    hi[i] = E::hi(v[i]);
+  }
+  write_half<E, T, MODE>(out, row, K, p0, lo, scale);
+  if (p0 + half < K) write_half<E, T, MODE>(out, row, K, p0 + half, hi, scale);
+}
+
+template <typename T, int G, int MODE, int UPT>
+__global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int64_t rows, int K, int half,
+                                                     void* __restrict__ out, float* __restrict__ scales) {
+  using E = Elem<T>;
+  using P = typename E::Pair;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  P* sm = reinterpret_cast<P*>(smem_raw);
+  __shared__ float red[32];
+
+  const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
+  const int units = half >> 4;
+  constexpr float kNorm = G == 1 ? 1.0f : G == 4 ? 0.5f : G == 16 ? 0.25f : G == 64 ? 0.125f : G == 256 ? 0.0625f : 0.03125f;
+  constexpr bool kSmem = G >= 64;  // later stages need other threads' words
+  const P nrm = E::splat(kNorm);
+
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const T* xr = x + row * static_cast<int64_t>(K);
+    float amax = 0.0f;
+
+    // phase 1: issue every load of this thread first, then rotate.
+    Raw16<T> rlo[UPT], rhi[UPT];
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+      const int u = tid + j * nthr;
+      if (u < units) {
+        const int p0 = u << 4;
+        load16(rlo[j], xr + p0);
+        if (p0 + half < K) load16(rhi[j], xr + p0 + half);
+        else zero16(rhi[j]);
+      }
+    }
+    P v[UPT][16];
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+      const int u = tid + j * nthr;
+      if (u < units) {
+        interleave<E>(v[j], rlo[j], rhi[j]);
+        stages_1_4<E, G>(v[j]);
+        if constexpr (!kSmem) {
+          if constexpr (G > 1) amax = normalize_absmax<E>(v[j], nrm, amax);
+          else amax = normalize_absmax<E>(v[j], E::splat(1.0f), amax);
+        } else {
+          const int p0 = u << 4;
+#pragma unroll
+          for (int m = 0; m < 4; ++m) st_chunk(sm, p0 + 4 * m, v[j][4 * m], v[j][4 * m + 1], v[j][4 * m + 2], v[j][4 * m + 3]);
+        }
+      }
+    }
+
+    if constexpr (kSmem) {
+      __syncthreads();
+      // phase 2
+#pragma unroll
+      for (int j = 0; j < UPT; ++j) {
+        const int t = tid + j * nthr;
+        if (t >= units) continue;
+        P w[16];
+        if constexpr (G == 64) {
+          const int q = t >> 2, k = t & 3;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ld_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) bfly4<E>(w[c], w[4 + c], w[8 + c], w[12 + c]);
+          amax = normalize_absmax<E>(w, nrm, amax);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) st_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        } else {
+          const int b = t >> 4, c = t & 15;
+          const int base = 256 * b + c;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = sm[swz(base + 16 * i)];
+          stages_1_4<E, 16>(w);
+          if constexpr (G == 256) amax = normalize_absmax<E>(w, nrm, amax);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sm[swz(base + 16 * i)] = w[i];
+        }
+      }
+      if constexpr (G == 1024) {
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < UPT; ++j) {
+          const int t = tid + j * nthr;
+          if (t >= units) continue;
+          P w[16];
+          const int q = t >> 6, c0 = (t & 63) << 2;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) ld_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) bfly4<E>(w[c], w[4 + c], w[8 + c], w[12 + c]);
+          amax = normalize_absmax<E>(w, nrm, amax);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) st_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+
+    float scale = 1.0f;
+    if constexpr (MODE != kModeRotate) {
+      // row absmax: warp shuffle, then across warps
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+      if ((tid & 31) == 0) red[tid >> 5] = amax;
+      __syncthreads();
+      if (tid < 32) {
+        float m = tid < (nthr >> 5) ? red[tid] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        if (tid == 0) red[0] = m;
+      }
+      __syncthreads();
+      const float floor_v = E::to_f(E::from_f(1.0e-10f));
+      const float maximum = E::to_f(E::from_f(fmaxf(red[0], floor_v)));
+      scale = E::to_f(E::from_f(__fdiv_rn(maximum, 7.0f)));
+      if (tid == 0) scales[row] = scale;
+    } else if constexpr (kSmem) {
+      __syncthreads();
+    }
+
+    // quantize (or emit the rotation)
+#pragma unroll
+    for (int j = 0; j < UPT; ++j) {
+      const int u = tid + j * nthr;
+      if (u >= units) continue;
+      const int p0 = u << 4;
+      if constexpr (kSmem) {
+        P w[16];
+#pragma unroll
+        for (int m = 0; m < 4; ++m) ld_chunk(sm, p0 + 4 * m, w[4 * m], w[4 * m + 1], w[4 * m + 2], w[4 * m + 3]);
+        emit_unit<E, T, MODE>(out, row, K, half, p0, w, scale);
+      } else {
+        emit_unit<E, T, MODE>(out, row, K, half, p0, v[j], scale);
+      }
+    }
+    if (row + gridDim.x < rows) __syncthreads();  // smem / red reuse by the next row
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host dispatch
+
+template <typename T, int G, int MODE>
+static int launch_g(const void* x, int64_t rows, int K, int half, void* out, float* scales, cudaStream_t stream) {
+  const int units = half / 16;
+  int upt = 1;
+  while (upt < 8 && (units + upt - 1) / upt > 256) upt *= 2;
+  int threads = ((units + upt - 1) / upt + 31) / 32 * 32;
+  CONVROT_REQUIRE(threads <= 256, CONVROT_ERR_UNSUPPORTED, "features %d too large for the fused kernel", K);
+  using P = typename Elem<T>::Pair;
+  const size_t smem = G >= 64 ? static_cast<size_t>(half) * sizeof(P) : 0;
+  CONVROT_REQUIRE(smem <= 227 * 1024, CONVROT_ERR_UNSUPPORTED, "features %d too large for the fused kernel", K);
+  if (rows == 0) return CONVROT_OK;
+  const unsigned grid = static_cast<unsigned>(rows < 2147483647LL ? rows : 2147483647LL);
+  auto run = [&](auto kernel) -> int {
+    if (smem > 48 * 1024) CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    kernel<<<grid, threads, smem, stream>>>(static_cast<const T*>(x), rows, K, half, out, scales);
+    return check_launch("convrot prep kernel");
+  };
+  switch (upt) {
+    case 1: return run(prep_kernel<T, G, MODE, 1>);
+    case 2: return run(prep_kernel<T, G, MODE, 2>);
+    case 4: return run(prep_kernel<T, G, MODE, 4>);
+    default: return run(prep_kernel<T, G, MODE, 8>);
+  }
+}
+
+template <typename T, int MODE>
+int launch_t(const void* x, int64_t rows, int64_t K, int G, void* out, float* scales, cudaStream_t stream) {
+  const int64_t groups = K / G;
+  const int64_t half = G == 1 ? K / 2 : ((groups + 1) / 2) * G;
+  CONVROT_REQUIRE(half % 16 == 0, CONVROT_ERR_UNSUPPORTED,
+                  "features %lld with group %d: the fused kernel needs half-rows of a multiple of 16 elements",
+                  static_cast<long long>(K), G);
+  CONVROT_REQUIRE(K <= (1 << 30), CONVROT_ERR_UNSUPPORTED, "features too large");
+  const int k = static_cast<int>(K), h = static_cast<int>(half);
+  switch (G) {
+    case 1: return launch_g<T, 1, MODE>(x, rows, k, h, out, scales, stream);
+    case 4: return launch_g<T, 4, MODE>(x, rows, k, h, out, scales, stream);
+    case 16: return launch_g<T, 16, MODE>(x, rows, k, h, out, scales, stream);
+    case 64: return launch_g<T, 64, MODE>(x, rows, k, h, out, scales, stream);
+    case 256: return launch_g<T, 256, MODE>(x, rows, k, h, out, scales, stream);
+    case 1024: return launch_g<T, 1024, MODE>(x, rows, k, h, out, scales, stream);
+    default: break;
+  }
+  set_error("group size %d is not supported (supported: 1, 4, 16, 64, 256, 1024)", G);
+  return CONVROT_ERR_UNSUPPORTED;
+}
+
+// Explicit instantiations live in prep_bf16.cu / prep_f16.cu / prep_f32.cu so
+// the three dtypes compile in parallel.
+#define CONVROT_PREP_INSTANTIATE(T)                                                                          \
+  template int launch_t<T, kModeI8>(const void*, int64_t, int64_t, int, void*, float*, cudaStream_t);     \
+  template int launch_t<T, kModePacked>(const void*, int64_t, int64_t, int, void*, float*, cudaStream_t); \
+  template int launch_t<T, kModeRotate>(const void*, int64_t, int64_t, int, void*, float*, cudaStream_t);
+
+}  // namespace convrot

@@ -1,0 +1,138 @@
+/*
+ * convrot_b200.h -- C ABI of libconvrot_b200.so, the sm_100a (B200) ConvRot
+ * W4A4 linear.
+ *
+ * Every entry point takes device pointers, element counts and a cudaStream_t
+ * (passed as void*, NULL = legacy default stream), enqueues its kernels on
+ * that stream and returns at once.  Nothing here allocates device memory: the
+ * caller owns every buffer.  Return value: CONVROT_OK (0) or a negative
+ * status; convrot_last_error() then gives a message (thread-local).
+ *
+ * Each function names the reference interface it replaces, as
+ * path:line in Lumenbeing/convrot-mlx (src/convrot_mlx/core.py).
+ *
+ * Conventions shared by all entry points
+ *   - matrices are row-major and densely packed (leading dimension = columns);
+ *   - "dtype" codes: CONVROT_F32, CONVROT_F16, CONVROT_BF16;
+ *   - int4 packing: two's-complement nibbles, element 2j in the low nibble
+ *     and 2j+1 in the high nibble of byte j (core.py:97-120);
+ *   - weight layouts: CONVROT_LAYOUT_NK = (N, K/2) bytes, packed along K
+ *     ("packed-nk-low-nibble-even-feature", core.py:1253-1254);
+ *     CONVROT_LAYOUT_KN = (K, N/2) bytes, packed along N
+ *     ("packed-kn-low-nibble-even-output", core.py:1248-1250).
+ */
+#ifndef CONVROT_B200_H
+#define CONVROT_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define CONVROT_OK 0
+#define CONVROT_ERR_INVALID (-1)     /* bad shape, pointer, alignment or argument */
+#define CONVROT_ERR_UNSUPPORTED (-2) /* valid for the reference, not for this build */
+#define CONVROT_ERR_CUDA (-3)        /* a CUDA runtime / driver call failed */
+
+/* dtype codes */
+#define CONVROT_F32 0
+#define CONVROT_F16 1
+#define CONVROT_BF16 2
+
+/* weight layouts */
+#define CONVROT_LAYOUT_NK 0
+#define CONVROT_LAYOUT_KN 1
+
+/* ABI version of this header (major * 100 + minor). */
+#define CONVROT_ABI_VERSION 100
+int convrot_abi_version(void);
+
+/* Message for the last non-zero status returned on this thread. */
+const char* convrot_last_error(void);
+
+/*
+ * Fused rotate + row quantize, int8 codes.
+ * Replaces metal_fused_prepare_convrot_activation_i8 (core.py:456-484; Metal
+ * kernel core.py:307-327).  x: (rows, features) of `dtype`; q_i8: (rows,
+ * features) int8 codes in [-7, 7]; scales: (rows,) float32 row scales.
+ * group_size in {16, 64, 256, 1024} (the reference fuses 64 and 256 and
+ * rotates any power of four eagerly, core.py:50-94); features % group_size == 0.
+ * group_size 1 skips the rotation (quantize_signed_int4_rowwise,
+ * core.py:149-158; then features % 32 == 0).
+ */
+int convrot_prepare_i8(const void* x, int dtype, int64_t rows, int64_t features,
+                       int group_size, int8_t* q_i8, float* scales, void* stream);
+
+/*
+ * Fused rotate + row quantize, packed int4 codes.
+ * Replaces metal_fused_prepare_convrot_activation (core.py:425-453; Metal
+ * kernel core.py:205-304), prepare_convrot_activation (core.py:161-167),
+ * compiled_prepare_convrot_activation (core.py:174) and, applied to a dense
+ * (out, in) weight, quantize_convrot_weight (core.py:514-527).
+ * q_packed: (rows, features / 2) bytes.
+ */
+int convrot_prepare_packed(const void* x, int dtype, int64_t rows, int64_t features,
+                           int group_size, uint8_t* q_packed, float* scales, void* stream);
+
+/*
+ * Normalized regular-Hadamard rotation only, output in the input dtype.
+ * Replaces metal_fused_rotate_convrot_activation (core.py:487-511; Metal
+ * kernel core.py:330-370) and regular_hadamard (core.py:64-94).
+ */
+int convrot_rotate(const void* x, int dtype, int64_t rows, int64_t features,
+                   int group_size, void* out, void* stream);
+
+/*
+ * Packed int4 -> int8.  Replaces metal_unpack_signed_int4 (core.py:1014-1027;
+ * Metal kernel core.py:915-922) and unpack_signed_int4 (core.py:108-120).
+ * packed: n_bytes bytes; out: 2 * n_bytes int8 values in [-8, 7].
+ */
+int convrot_unpack_int4(const uint8_t* packed, int64_t n_bytes, int8_t* out, void* stream);
+
+/*
+ * int8 -> packed int4 (values are taken modulo 16).  Replaces
+ * pack_signed_int4 (core.py:97-105).  n_values must be even.
+ */
+int convrot_pack_int4(const int8_t* values, int64_t n_values, uint8_t* out, void* stream);
+
+/*
+ * Transpose a packed (rows, 2 * packed_cols) int4 matrix into a packed
+ * (2 * packed_cols, rows) one: NK -> KN (repack_nk_weight_for_mpp,
+ * core.py:123-133) and KN -> NK (repack_mpp_weight_to_nk, core.py:136-146).
+ * rows must be even.  out: (2 * packed_cols, rows / 2) bytes.
+ */
+int convrot_repack_int4_transpose(const uint8_t* in, int64_t rows, int64_t packed_cols,
+                                  uint8_t* out, void* stream);
+
+/*
+ * W4A4 linear: out[m, n] = T(float(sum_k a[m,k] w[n,k]) * xscales[m] *
+ * wscales[n] + bias[n]) with an exact int32 dot (tcgen05 kind::i8) and the
+ * epilogue fused.  Replaces mpp_w4a4_int8_matmul (core.py:1088-1120; Metal
+ * K6 core.py:839-874 + epilogue K9 core.py:925-937), and, with layout NK,
+ * the math of packed_w4a4_matmul* (core.py:745-828), expanded_fp32 /
+ * reference_w4a4_matmul (core.py:1155-1207).
+ * act: (m, k) int8 codes; qweight: packed `layout`; xscales (m,), wscales
+ * (n,), bias (n,) float32 (bias may be NULL = zeros); out: (m, n) of
+ * out_dtype.  k % 32 == 0; layout KN needs n even.
+ */
+int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout,
+                      const float* xscales, const float* wscales, const float* bias,
+                      void* out, int out_dtype, int64_t m, int64_t n, int64_t k,
+                      void* stream);
+
+/*
+ * Diagnostics: every wait inside the tcgen05 kernels is bounded; a kernel
+ * whose wait times out stops early and records a non-zero code in a
+ * device-side word.  This reads and clears that word (0 = no time-out).  It
+ * synchronizes the current device.  No reference counterpart (the reference
+ * has no failure detection beyond shape checks).
+ */
+int convrot_take_device_error(int* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CONVROT_B200_H */

@@ -130,7 +130,9 @@ __device__ __forceinline__ void item_geometry(const Params& p, int item, int n0,
     const int q = (lane & 3) + 4 * (lane >> 4);
     const int gk = k0 + kr, gn = n0 + 32 * q;
     goff = (gk < p.K && gn < p.N) ? static_cast<int64_t>(gk) * (p.N >> 1) + (gn >> 1) : -1;
-    vec_ok = ((p.N & 31) == 0) || (gn + 32 <= p.N);
+    // 16-byte loads need a row stride (N / 2 bytes) that is a multiple of 16;
+    // then every item with gn < N also lies wholly inside the row.
+    vec_ok = (p.N & 31) == 0;
     const uint32_t base = (q >> 2) * (BK * 128) + (kr >> 3) * 1024 + (kr & 7) * 128;
     const int c = 2 * (q & 3);
     s0 = base + ((c ^ (kr & 7)) << 4);

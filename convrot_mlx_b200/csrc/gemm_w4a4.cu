@@ -59,7 +59,8 @@ struct alignas(8) Barriers {
   int err;
 };
 
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBBytes) + sizeof(Barriers);
+constexpr int kEpiBytes = kEpiWarps * 2 * BN * 4;  // ws and bias, one copy per epilogue warp
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBBytes) + kEpiBytes + sizeof(Barriers);
 
 struct Params {
   const uint8_t* qweight;
@@ -111,63 +112,87 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
-// Location of transform item `item` of a stage: global byte offset (or -1 when
-// it lies outside the weight) and the two smem chunk offsets of its 32 bytes.
+// Per-thread description of one transform item: 16 packed bytes (32 int4
+// values) that become 32 int8 bytes in two 16-byte chunks of a B stage.
+// Everything but the block origin (n0, k0) is fixed for the whole kernel.
+struct Item {
+  int a;          // NK: row n within the tile;   KN: row k within the block
+  int b;          // NK: 32-k group q (0..3);     KN: 32-n group q (0..7)
+  uint32_t s0;    // smem offsets of the two output chunks within a stage
+  uint32_t s1;
+};
+
 template <int LAYOUT>
-__device__ __forceinline__ void item_geometry(const Params& p, int item, int n0, int k0, int64_t& goff, bool& vec_ok,
-                                              uint32_t& s0, uint32_t& s1) {
+__device__ __forceinline__ Item make_item(int item) {
+  Item it;
   if constexpr (LAYOUT == CONVROT_LAYOUT_NK) {
+    // K-major 128-byte-swizzled tile: row n at n * 128, chunk c at (c ^ (n & 7)) * 16
     const int n = item >> 2, q = item & 3;
-    const int gn = n0 + n, gk = k0 + 32 * q;
-    goff = (gn < p.N && gk < p.K) ? static_cast<int64_t>(gn) * (p.K >> 1) + (gk >> 1) : -1;
-    vec_ok = true;
-    const uint32_t row = (n >> 3) * 1024 + (n & 7) * 128;
-    s0 = row + (((2 * q) ^ (n & 7)) << 4);
-    s1 = row + (((2 * q + 1) ^ (n & 7)) << 4);
+    it.a = n;
+    it.b = q;
+    const uint32_t row = n * 128;
+    it.s0 = row + (((2 * q) ^ (n & 7)) << 4);
+    it.s1 = row + (((2 * q + 1) ^ (n & 7)) << 4);
   } else {
+    // MN-major 128-byte-swizzled tile: n-atoms of 128 columns (BK * 128 bytes
+    // apart), each 8-row k-atoms of 1 KB; chunk c of row k at (c ^ (k & 7)) * 16.
+    // Lanes 0-3 / 4-7 of a quarter-warp take two consecutive k rows so their
+    // eight chunks fall on distinct banks.
     const int wi = item >> 5, lane = item & 31;
     const int kr = 4 * wi + ((lane >> 2) & 3);
     const int q = (lane & 3) + 4 * (lane >> 4);
-    const int gk = k0 + kr, gn = n0 + 32 * q;
-    goff = (gk < p.K && gn < p.N) ? static_cast<int64_t>(gk) * (p.N >> 1) + (gn >> 1) : -1;
-    // 16-byte loads need a row stride (N / 2 bytes) that is a multiple of 16;
-    // then every item with gn < N also lies wholly inside the row.
-    vec_ok = (p.N & 31) == 0;
+    it.a = kr;
+    it.b = q;
     const uint32_t base = (q >> 2) * (BK * 128) + (kr >> 3) * 1024 + (kr & 7) * 128;
     const int c = 2 * (q & 3);
-    s0 = base + ((c ^ (kr & 7)) << 4);
-    s1 = base + (((c + 1) ^ (kr & 7)) << 4);
+    it.s0 = base + ((c ^ (kr & 7)) << 4);
+    it.s1 = base + (((c + 1) ^ (kr & 7)) << 4);
   }
+  return it;
 }
 
+// Load the 16 packed bytes of `it` for the block at (n0, k0); zero outside the weight.
 template <int LAYOUT>
-__device__ __forceinline__ uint4 load_item(const Params& p, int64_t goff, bool vec_ok, int gn_base) {
-  if (goff < 0) return make_uint4(0, 0, 0, 0);
-  const uint8_t* src = p.qweight + goff;
-  if (LAYOUT == CONVROT_LAYOUT_NK || vec_ok) return __ldg(reinterpret_cast<const uint4*>(src));
-  // KN item crossing the N edge (N % 32 != 0): bytes one by one, zero past N.
-  uint32_t w[4] = {0, 0, 0, 0};
-  for (int b = 0; b < 16; ++b) {
-    if (gn_base + 2 * b < p.N) w[b >> 2] |= static_cast<uint32_t>(src[b]) << (8 * (b & 3));
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
-}
-
-template <int LAYOUT>
-__device__ __forceinline__ int item_gn(int item, int n0) {
+__device__ __forceinline__ uint4 load_item(const Params& p, const Item& it, int n0, int k0) {
   if constexpr (LAYOUT == CONVROT_LAYOUT_NK) {
-    return n0;
+    const int gn = n0 + it.a, gk = k0 + 32 * it.b;
+    if (gn >= p.N || gk >= p.K) return make_uint4(0, 0, 0, 0);
+    // K % 32 == 0: the row stride K / 2 and the offset gk / 2 are multiples of 16
+    return __ldg(reinterpret_cast<const uint4*>(p.qweight + static_cast<int64_t>(gn) * (p.K >> 1) + (gk >> 1)));
   } else {
-    const int lane = item & 31;
-    return n0 + 32 * ((lane & 3) + 4 * (lane >> 4));
+    const int gk = k0 + it.a, gn = n0 + 32 * it.b;
+    if (gk >= p.K || gn >= p.N) return make_uint4(0, 0, 0, 0);
+    const uint8_t* src = p.qweight + static_cast<int64_t>(gk) * (p.N >> 1) + (gn >> 1);
+    // 16-byte loads need a row stride (N / 2 bytes) that is a multiple of 16;
+    // then every item with gn < N also lies wholly inside the row.
+    if ((p.N & 31) == 0) return __ldg(reinterpret_cast<const uint4*>(src));
+    // ragged N: bytes one by one, zero past N (byte b holds columns gn + 2b, gn + 2b + 1)
+    uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+      const uint32_t v = (gn + 2 * b < p.N) ? static_cast<uint32_t>(src[b]) << (8 * (b & 3)) : 0u;
+      if (b < 4) w0 |= v;
+      else if (b < 8) w1 |= v;
+      else if (b < 12) w2 |= v;
+      else w3 |= v;
+    }
+    return make_uint4(w0, w1, w2, w3);
   }
+}
+
+template <int LAYOUT>
+__device__ __forceinline__ void load_block(const Params& p, const Item (&it)[kItemsPerThread], int tile, int kb,
+                                           uint4 (&dst)[kItemsPerThread]) {
+  const int n0 = (tile / p.m_tiles) * BN, k0 = kb * BK;
+#pragma unroll
+  for (int i = 0; i < kItemsPerThread; ++i) dst[i] = load_item<LAYOUT>(p, it[i], n0, k0);
 }
 
 // 16 consecutive outputs with 16-byte stores (pointer 16-byte aligned).
-__device__ __forceinline__ void store16(float* dst, const float (&v)[16]) {
+__device__ __forceinline__ void store16(float* dst, const float (&v)[32], int o) {
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    reinterpret_cast<float4*>(dst)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    reinterpret_cast<float4*>(dst)[q] = make_float4(v[o + 4 * q], v[o + 4 * q + 1], v[o + 4 * q + 2], v[o + 4 * q + 3]);
 }
 
 template <typename T16>
@@ -178,11 +203,12 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 }
 
 template <typename T16>
-__device__ __forceinline__ void store16(T16* dst, const float (&v)[16]) {
+__device__ __forceinline__ void store16(T16* dst, const float (&v)[32], int o) {
 #pragma unroll
   for (int q = 0; q < 2; ++q)
-    reinterpret_cast<uint4*>(dst)[q] = make_uint4(pack2<T16>(v[8 * q], v[8 * q + 1]), pack2<T16>(v[8 * q + 2], v[8 * q + 3]),
-                                                  pack2<T16>(v[8 * q + 4], v[8 * q + 5]), pack2<T16>(v[8 * q + 6], v[8 * q + 7]));
+    reinterpret_cast<uint4*>(dst)[q] =
+        make_uint4(pack2<T16>(v[o + 8 * q], v[o + 8 * q + 1]), pack2<T16>(v[o + 8 * q + 2], v[o + 8 * q + 3]),
+                   pack2<T16>(v[o + 8 * q + 4], v[o + 8 * q + 5]), pack2<T16>(v[o + 8 * q + 6], v[o + 8 * q + 7]));
 }
 
 template <int LAYOUT, typename TOut>
@@ -192,7 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * kABytes;
-  Barriers* bars = reinterpret_cast<Barriers*>(sB + STAGES * kBBytes);
+  float* epi_ws = reinterpret_cast<float*>(sB + STAGES * kBBytes);
+  Barriers* bars = reinterpret_cast<Barriers*>(sB + STAGES * kBBytes + kEpiBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -226,9 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      int issued[STAGES];
-      uint32_t issued_phase[STAGES];
-      for (int s = 0; s < STAGES; ++s) issued[s] = 0;
+      int issued = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int m_blk = tile % p.m_tiles;
@@ -236,15 +261,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wait_bar(&bars->empty[stage], phase ^ 1, bars, 1)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->a_full[stage], kABytes);
           tma_load_2d(sA + stage * kABytes, &tmap_a, &bars->a_full[stage], kb * BK, m_blk * BM);
-          issued[stage] = 1;
-          issued_phase[stage] = phase;
+          ++issued;
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
       }
       if (!ok) {
-        // error exit: let the copies already in flight land before the CTA ends
-        for (int s = 0; s < STAGES; ++s)
-          if (issued[s]) wait_bar(&bars->a_full[s], issued_phase[s], bars, 1);
+        // error exit: let the (at most STAGES) copies still in flight land
+        for (int j = 0; j < STAGES && j < issued; ++j) {
+          if (--stage < 0) { stage = STAGES - 1; phase ^= 1; }
+          wait_bar(&bars->a_full[stage], phase, bars, 1);
+        }
       }
     }
   } else if (warp == kWarpMma) {
@@ -291,94 +317,107 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp < kWarpEpi0) {
     // ---------------- weight transform ----------------
+    // Blocks (tile, kb) in this CTA's order; registers hold the packed bytes of
+    // the current block and the two after it, so global latency is covered by
+    // two blocks of tensor-core work.
     const int xt = threadIdx.x - kWarpXform0 * 32;
+    Item it[kItemsPerThread];
+#pragma unroll
+    for (int i = 0; i < kItemsPerThread; ++i) it[i] = make_item<LAYOUT>(i * kXformThreads + xt);
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true;
-    uint4 cur[kItemsPerThread], nxt[kItemsPerThread];
-    int64_t goff[kItemsPerThread];
-    bool vec_ok[kItemsPerThread];
-    uint32_t s0[kItemsPerThread], s1[kItemsPerThread];
-    // block sequence of this CTA: (tile, kb) pairs; prefetch one block ahead
-    int tile = blockIdx.x, kb = 0;
-    auto issue = [&](int t, int k, uint4 (&dst)[kItemsPerThread]) {
-      const int n0 = (t / p.m_tiles) * BN;
-#pragma unroll
-      for (int i = 0; i < kItemsPerThread; ++i) {
-        const int item = i * kXformThreads + xt;
-        int64_t g;
-        bool v;
-        uint32_t a0, a1;
-        item_geometry<LAYOUT>(p, item, n0, k * BK, g, v, a0, a1);
-        dst[i] = load_item<LAYOUT>(p, g, v, item_gn<LAYOUT>(item, n0));
-      }
+    uint4 b0[kItemsPerThread], b1[kItemsPerThread], b2[kItemsPerThread];
+    int t0 = blockIdx.x, k0 = 0;         // block being written
+    int t1 = t0, k1 = 0, t2 = t0, k2 = 0;  // the next two blocks
+    auto advance = [&](int& t, int& k) {
+      if (++k == p.k_blocks) { k = 0; t += gridDim.x; }
     };
-    if (tile < num_tiles) issue(tile, 0, cur);
-    while (tile < num_tiles && ok) {
-      int ntile = tile, nkb = kb + 1;
-      if (nkb == p.k_blocks) { nkb = 0; ntile += gridDim.x; }
-      if (ntile < num_tiles) issue(ntile, nkb, nxt);
-      const int n0 = (tile / p.m_tiles) * BN;
-#pragma unroll
-      for (int i = 0; i < kItemsPerThread; ++i) {
-        const int item = i * kXformThreads + xt;
-        item_geometry<LAYOUT>(p, item, n0, kb * BK, goff[i], vec_ok[i], s0[i], s1[i]);
-      }
-      if (!wait_bar(&bars->empty[stage], phase ^ 1, bars, 6)) { ok = false; break; }
+    t1 = t0; k1 = k0; advance(t1, k1);
+    t2 = t1; k2 = k1; advance(t2, k2);
+    if (t0 < num_tiles) load_block<LAYOUT>(p, it, t0, k0, b0);
+    if (t1 < num_tiles) load_block<LAYOUT>(p, it, t1, k1, b1);
+    while (t0 < num_tiles) {
+      if (t2 < num_tiles) load_block<LAYOUT>(p, it, t2, k2, b2);
+      if (!wait_bar(&bars->empty[stage], phase ^ 1, bars, 6)) break;
       const uint32_t b_addr = smem_u32(sB + stage * kBBytes);
 #pragma unroll
       for (int i = 0; i < kItemsPerThread; ++i) {
         uint32_t o[8];
-        expand16(cur[i], o);
-        sts128(b_addr + s0[i], o[0], o[1], o[2], o[3]);
-        sts128(b_addr + s1[i], o[4], o[5], o[6], o[7]);
+        expand16(b0[i], o);
+        sts128(b_addr + it[i].s0, o[0], o[1], o[2], o[3]);
+        sts128(b_addr + it[i].s1, o[4], o[5], o[6], o[7]);
       }
       fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->b_full[stage]);
       if (++stage == STAGES) { stage = 0; phase ^= 1; }
 #pragma unroll
-      for (int i = 0; i < kItemsPerThread; ++i) cur[i] = nxt[i];
-      tile = ntile;
-      kb = nkb;
+      for (int i = 0; i < kItemsPerThread; ++i) {
+        b0[i] = b1[i];
+        b1[i] = b2[i];
+      }
+      t0 = t1; k0 = k1;
+      t1 = t2; k1 = k2;
+      advance(t2, k2);
     }
   } else {
     // ---------------- epilogue ----------------
+    // Each epilogue warp stages the tile columns' weight scales and bias in its
+    // own shared-memory slice (only warp-level synchronization, so a warp that
+    // stops early on an error can never strand the others); each thread owns
+    // one output row and reads 32 accumulator columns per tcgen05.ld.
     const int ew = warp & 3;  // TMEM lane quarter this warp may access
+    float* sws = epi_ws + ew * 2 * BN;
+    float* sbias = sws + BN;
     int local = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
-      if (!wait_bar(&bars->acc_full[buf], acc_phase, bars, 7)) { ok = false; break; }
+      __syncwarp();  // the previous tile's reads of sws / sbias are done
+      for (int j = lane; j < BN; j += 32) {
+        const int col = n_blk * BN + j;
+        sws[j] = col < p.N ? __ldg(p.wscales + col) : 0.0f;
+        sbias[j] = (col < p.N && p.bias) ? __ldg(p.bias + col) : 0.0f;
+      }
+      __syncwarp();
+      if (!wait_bar(&bars->acc_full[buf], acc_phase, bars, 7)) break;
       tc_fence_after();
       const int m = m_blk * BM + ew * 32 + lane;
       const bool row_ok = m < p.M;
       const float xs = row_ok ? __ldg(p.xscales + m) : 0.0f;
       TOut* orow = static_cast<TOut*>(p.out) + static_cast<int64_t>(row_ok ? m : 0) * p.N;
       const bool vec_store = (p.N % (16 / sizeof(TOut))) == 0;
-      for (int c = 0; c < BN / 16; ++c) {
-        const int n = n_blk * BN + c * 16;
-        uint32_t r[16];
+      const uint32_t t_row = tmem_base + ((ew * 32u) << 16) + buf * BN;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n = n_blk * BN + c * 32;
+        if (n >= p.N) break;  // uniform across the warp
+        uint32_t r[32];
         __syncwarp();  // tcgen05.ld is .sync.aligned: the whole warp, converged
-        tmem_ld_32x32b_x16(tmem_base + ((ew * 32u) << 16) + buf * BN + c * 16, r);
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
-        if (n >= p.N) continue;
-        float v[16];
+        float v[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int col = min(n + j, p.N - 1);
-          const float ws = __ldg(p.wscales + col);
-          const float bb = p.bias ? __ldg(p.bias + col) : 0.0f;
-          const float dot = static_cast<float>(static_cast<int32_t>(r[j]) >> 4);
-          v[j] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), ws), bb);
+        for (int j = 0; j < 32; j += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
+          const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            // accumulator = 16 * dot exactly; dot * xs * ws + bias, each step rounded
+            const float dot = static_cast<float>(static_cast<int32_t>(r[j + u]) >> 4);
+            v[j + u] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), wv[u]), bv[u]);
+          }
         }
         if (!row_ok) continue;
-        if (vec_store && n + 16 <= p.N) {
-          store16(orow + n, v);
+        if (vec_store && n + 32 <= p.N) {
+          store16(orow + n, v, 0);
+          store16(orow + n + 16, v, 16);
         } else {
-          for (int j = 0; j < 16 && n + j < p.N; ++j) orow[n + j] = cvt_out<TOut>(v[j]);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < p.N) orow[n + j] = cvt_out<TOut>(v[j]);
         }
       }
       tc_fence_before();

@@ -19,6 +19,8 @@
 // then x / sqrt(G) (exact), scale = T(T(max(absmax, T(1e-10))) / 7) and
 // code = clamp(rint(T(x / scale)), -7, 7) (core.py:149-158, :258-298).
 #pragma once
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace convrot {
@@ -34,15 +36,25 @@ __device__ __forceinline__ int swz(int p) {
   return (r << 5) | ((((p >> 2) & 7) ^ h) << 2) | (p & 3);
 }
 
-template <typename E, typename P>
+// One radix-4 butterfly on pair-words.  kExact keeps even the sign of a zero
+// result identical to the reference ((-a) + b is computed as b - a); the
+// quantizing modes use (c - (a - b)) + d instead, one op fewer, which can
+// differ from it only in the sign of an exact zero -- invisible after abs and
+// rint.
+template <typename E, bool kExact = true, typename P>
 __device__ __forceinline__ void bfly4(P& a, P& b, P& c, P& d) {
   const P s = E::add(a, b);
   const P t = E::sub(a, b);
-  const P u = E::sub(b, a);  // == (-a) + b, including the sign of zero
   const P o0 = E::sub(E::add(s, c), d);
   const P o1 = E::add(E::sub(s, c), d);
   const P o2 = E::add(E::add(t, c), d);
-  const P o3 = E::add(E::add(u, c), d);
+  P o3;
+  if constexpr (kExact) {
+    const P u = E::sub(b, a);  // == (-a) + b, including the sign of zero
+    o3 = E::add(E::add(u, c), d);
+  } else {
+    o3 = E::add(E::sub(c, t), d);
+  }
   a = o0;
   b = o1;
   c = o2;
@@ -115,16 +127,27 @@ __device__ __forceinline__ void interleave(P (&v)[16], const Raw16<T>& lo, const
 }
 
 // Radix-4 stages with strides 1 and 4 over 16 registers (stride 1 only for G == 4).
-template <typename E, int G, typename P>
+template <typename E, int G, bool kExact, typename P>
 __device__ __forceinline__ void stages_1_4(P (&v)[16]) {
   if constexpr (G >= 4) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) bfly4<E>(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    for (int j = 0; j < 4; ++j) bfly4<E, kExact>(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
   if constexpr (G >= 16) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) bfly4<E>(v[j], v[j + 4], v[j + 8], v[j + 12]);
+    for (int j = 0; j < 4; ++j) bfly4<E, kExact>(v[j], v[j + 4], v[j + 8], v[j + 12]);
   }
+}
+
+// bf16 quantizing modes skip the explicit x / sqrt(G) (a power of two: exact
+// unless the value underflows, and then its code is 0 either way) and fold it
+// into the reciprocal scale; the row absmax runs on packed bf16x2 words.
+template <typename T, int MODE>
+constexpr bool kFastQuant = std::is_same<T, __nv_bfloat16>::value && MODE != kModeRotate;
+
+__device__ __forceinline__ void absmax_bf16x2(const __nv_bfloat162 (&v)[16], __nv_bfloat162& m) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = __hmax2(m, __habs2(v[i]));
 }
 
 template <typename E, typename P>
@@ -179,6 +202,62 @@ __device__ __forceinline__ void write_half(void* out, int64_t row, int64_t K, in
   }
 }
 
+// bf16 codes of two elements.  With r = fl(1 / scale) (times the exact
+// 2^-k normalization), RNE_bf16(fl(x * r)) == RNE_bf16(x / scale) for bf16 x
+// and scale: a quotient of 8-bit significands is never a bf16 midpoint (its
+// odd part would need >= 9 bits) and lies >= 2^-17 (relative) from every
+// midpoint, while fl(x * r) is within 2^-23 of it.  Adding 136 in bf16 (ulp 1
+// on [128, 256)) then rounds half-to-even to an integer and leaves 8 + code
+// (code in [-7, 7]) in the low byte of each half.
+__device__ __forceinline__ uint32_t codes2_bf16(__nv_bfloat162 v, float r) {
+  const uint32_t bits = *reinterpret_cast<const uint32_t*>(&v);
+  const float x0 = __uint_as_float(bits << 16);
+  const float x1 = __uint_as_float(bits & 0xFFFF0000u);
+  const __nv_bfloat162 q = __floats2bfloat162_rn(__fmul_rn(x0, r), __fmul_rn(x1, r));
+  const __nv_bfloat162 t = __hadd2(q, __float2bfloat162_rn(136.0f));
+  return *reinterpret_cast<const uint32_t*>(&t);
+}
+
+template <int MODE>
+__device__ __forceinline__ void emit_unit_bf16(void* out, int64_t row, int64_t K, int half, int p0,
+                                               const __nv_bfloat162 (&v)[16], float r) {
+  uint32_t lo[4], hi[4];  // biased codes 8 + c, one per byte, elements p0.. and p0 + half..
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t t0 = codes2_bf16(v[4 * j], r), t1 = codes2_bf16(v[4 * j + 1], r);
+    const uint32_t t2 = codes2_bf16(v[4 * j + 2], r), t3 = codes2_bf16(v[4 * j + 3], r);
+    const uint32_t x = __byte_perm(t0, t1, 0x6240);  // lo0 lo1 hi0 hi1
+    const uint32_t y = __byte_perm(t2, t3, 0x6240);
+    lo[j] = __byte_perm(x, y, 0x5410);
+    hi[j] = __byte_perm(x, y, 0x7632);
+  }
+  const bool hi_ok = p0 + half < K;
+  if constexpr (MODE == kModeI8) {
+    // byte 8 + c -> two's-complement c: (u + 0x78) ^ 0x80, no carry across bytes
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      lo[j] = (lo[j] + 0x78787878u) ^ 0x80808080u;
+      hi[j] = (hi[j] + 0x78787878u) ^ 0x80808080u;
+    }
+    int8_t* o = static_cast<int8_t*>(out) + row * K;
+    *reinterpret_cast<uint4*>(o + p0) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    if (hi_ok) *reinterpret_cast<uint4*>(o + p0 + half) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  } else {
+    // nibble = (8 + c) ^ 8; two nibbles per byte, element 2j low
+    uint32_t pl[2], ph[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint32_t a0 = lo[2 * j] ^ 0x08080808u, a1 = lo[2 * j + 1] ^ 0x08080808u;
+      const uint32_t b0 = hi[2 * j] ^ 0x08080808u, b1 = hi[2 * j + 1] ^ 0x08080808u;
+      pl[j] = __byte_perm((a0 | (a0 >> 4)) & 0x00FF00FFu, (a1 | (a1 >> 4)) & 0x00FF00FFu, 0x6420);
+      ph[j] = __byte_perm((b0 | (b0 >> 4)) & 0x00FF00FFu, (b1 | (b1 >> 4)) & 0x00FF00FFu, 0x6420);
+    }
+    uint8_t* o = static_cast<uint8_t*>(out) + row * (K / 2);
+    *reinterpret_cast<uint2*>(o + p0 / 2) = make_uint2(pl[0], pl[1]);
+    if (hi_ok) *reinterpret_cast<uint2*>(o + (p0 + half) / 2) = make_uint2(ph[0], ph[1]);
+  }
+}
+
 template <typename E, typename T, int MODE, typename P>
 __device__ __forceinline__ void emit_unit(void* out, int64_t row, int64_t K, int half, int p0, const P (&v)[16],
                                           float scale) {
@@ -206,11 +285,24 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
   const int units = half >> 4;
   constexpr float kNorm = G == 1 ? 1.0f : G == 4 ? 0.5f : G == 16 ? 0.25f : G == 64 ? 0.125f : G == 256 ? 0.0625f : 0.03125f;
   constexpr bool kSmem = G >= 64;  // later stages need other threads' words
+  constexpr bool kFast = kFastQuant<T, MODE>;
+  constexpr bool kExact = !kFast;
   const P nrm = E::splat(kNorm);
 
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + row * static_cast<int64_t>(K);
     float amax = 0.0f;
+    P amax2 = E::splat(0.0f);  // fast path: packed running max of |x|
+    // last-stage bookkeeping: normalize + absmax (generic) or packed absmax (fast)
+    auto finish = [&](P (&w)[16]) {
+      if constexpr (kFast) {
+        absmax_bf16x2(w, amax2);
+      } else if constexpr (G > 1) {
+        amax = normalize_absmax<E>(w, nrm, amax);
+      } else {
+        amax = normalize_absmax<E>(w, E::splat(1.0f), amax);
+      }
+    };
 
     // phase 1: issue every load of this thread first, then rotate.
     Raw16<T> rlo[UPT], rhi[UPT];
@@ -230,10 +322,9 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
       const int u = tid + j * nthr;
       if (u < units) {
         interleave<E>(v[j], rlo[j], rhi[j]);
-        stages_1_4<E, G>(v[j]);
+        stages_1_4<E, G, kExact>(v[j]);
         if constexpr (!kSmem) {
-          if constexpr (G > 1) amax = normalize_absmax<E>(v[j], nrm, amax);
-          else amax = normalize_absmax<E>(v[j], E::splat(1.0f), amax);
+          finish(v[j]);
         } else {
           const int p0 = u << 4;
 #pragma unroll
@@ -255,8 +346,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
 #pragma unroll
           for (int i = 0; i < 4; ++i) ld_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) bfly4<E>(w[c], w[4 + c], w[8 + c], w[12 + c]);
-          amax = normalize_absmax<E>(w, nrm, amax);
+          for (int c = 0; c < 4; ++c) bfly4<E, kExact>(w[c], w[4 + c], w[8 + c], w[12 + c]);
+          finish(w);
 #pragma unroll
           for (int i = 0; i < 4; ++i) st_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         } else {
@@ -264,8 +355,8 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
           const int base = 256 * b + c;
 #pragma unroll
           for (int i = 0; i < 16; ++i) w[i] = sm[swz(base + 16 * i)];
-          stages_1_4<E, 16>(w);
-          if constexpr (G == 256) amax = normalize_absmax<E>(w, nrm, amax);
+          stages_1_4<E, 16, kExact>(w);
+          if constexpr (G == 256) finish(w);
 #pragma unroll
           for (int i = 0; i < 16; ++i) sm[swz(base + 16 * i)] = w[i];
         }
@@ -281,16 +372,20 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
 #pragma unroll
           for (int i = 0; i < 4; ++i) ld_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) bfly4<E>(w[c], w[4 + c], w[8 + c], w[12 + c]);
-          amax = normalize_absmax<E>(w, nrm, amax);
+          for (int c = 0; c < 4; ++c) bfly4<E, kExact>(w[c], w[4 + c], w[8 + c], w[12 + c]);
+          finish(w);
 #pragma unroll
           for (int i = 0; i < 4; ++i) st_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
 
-    float scale = 1.0f;
+    float scale = 1.0f, rscale = 1.0f;
     if constexpr (MODE != kModeRotate) {
+      if constexpr (kFast) {
+        // |x| of the unnormalized rotation; x / sqrt(G) is an exact power-of-two scale
+        amax = fmaxf(__low2float(amax2), __high2float(amax2)) * kNorm;
+      }
       // row absmax: warp shuffle, then across warps
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
@@ -306,6 +401,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
       const float floor_v = E::to_f(E::from_f(1.0e-10f));
       const float maximum = E::to_f(E::from_f(fmaxf(red[0], floor_v)));
       scale = E::to_f(E::from_f(__fdiv_rn(maximum, 7.0f)));
+      rscale = __fdiv_rn(1.0f, scale) * kNorm;
       if (tid == 0) scales[row] = scale;
     } else if constexpr (kSmem) {
       __syncthreads();
@@ -321,9 +417,11 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
         P w[16];
 #pragma unroll
         for (int m = 0; m < 4; ++m) ld_chunk(sm, p0 + 4 * m, w[4 * m], w[4 * m + 1], w[4 * m + 2], w[4 * m + 3]);
-        emit_unit<E, T, MODE>(out, row, K, half, p0, w, scale);
+        if constexpr (kFast) emit_unit_bf16<MODE>(out, row, K, half, p0, w, rscale);
+        else emit_unit<E, T, MODE>(out, row, K, half, p0, w, scale);
       } else {
-        emit_unit<E, T, MODE>(out, row, K, half, p0, v[j], scale);
+        if constexpr (kFast) emit_unit_bf16<MODE>(out, row, K, half, p0, v[j], rscale);
+        else emit_unit<E, T, MODE>(out, row, K, half, p0, v[j], scale);
       }
     }
     if (row + gridDim.x < rows) __syncthreads();  // smem / red reuse by the next row

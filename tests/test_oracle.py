@@ -195,3 +195,29 @@ def test_group_size_validation():
             O.validate_group_size(bad)
     for good in (4, 16, 64, 256, 1024):
         O.validate_group_size(good)
+
+
+def test_torch_cpu_port_matches_oracle():
+    # the timed CPU baseline (oracle/torch_cpu.py) must be the same contract, bit for bit
+    import torch
+
+    from oracle import torch_cpu as TC
+
+    rng = np.random.default_rng(99)
+    for k, g in ((512, 256), (2688, 64), (3072, 256)):
+        x = O.round_bf16(rng.normal(size=(33, k)).astype(np.float32))
+        x[:, rng.choice(k, 5, replace=False)] *= 20.0
+        x = O.round_bf16(x)
+        xt = torch.from_numpy(x).to(torch.bfloat16)
+        codes, scales = TC.prepare(xt, g)
+        ec, es = O.prepare_convrot_activation_i8(x, g)
+        np.testing.assert_array_equal(codes.numpy(), ec)
+        np.testing.assert_array_equal(scales.numpy(), es)
+        w = O.round_bf16((rng.normal(size=(40, k)) * 0.02).astype(np.float32))
+        qw, ws = O.quantize_convrot_weight(w, g)
+        b = rng.normal(size=40).astype(np.float32)
+        out = TC.linear(xt, torch.from_numpy(qw), torch.from_numpy(ws), torch.from_numpy(b), g)
+        expected = O.convrot_linear_w4a4(x, qw, "nk", ws, b, g)
+        np.testing.assert_array_equal(out.view(torch.int16).numpy().view(np.uint16), O.bf16_bits(expected))
+        np.testing.assert_array_equal(TC.pack(torch.from_numpy(ec)).numpy(), O.pack_signed_int4(ec))
+        np.testing.assert_array_equal(TC.unpack(torch.from_numpy(qw)).numpy(), O.unpack_signed_int4(qw))

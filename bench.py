@@ -12,9 +12,10 @@ is whole-job throughput in tera int-ops/s (2 M N K per linear).  One JSON line
 is printed by rank 0.
 
 Timing: the step is captured once as a CUDA graph (12 prep + 12 GEMM launches)
-and replayed; CUDA events recorded inside the graph time every kernel on its
-own stream.  The per-step working set (~1.2 GB) is ~10x the 126 MB L2, and no
-two consecutive linears share an operand, so every linear reads cold inputs.
+and replayed K times between CUDA events on its stream.  The rooflines come
+from graphs of the 12 GEMMs alone and the 12 preps alone, timed the same way.
+The per-step working set (~1.2 GB) is ~10x the 126 MB L2, and no two
+consecutive linears share an operand, so every linear reads cold inputs.
 ``e2e`` is the same metric through the public API (``ConvRotLinear``) with
 host buffers: pinned host -> device copy of each input and device -> host copy
 of each output inside the timed region.  ``--impl reference`` times the
@@ -98,19 +99,19 @@ def max_over_ranks(value: float, world: int) -> float:
 class ClockSampler:
     """nvidia-smi samples (200 ms) of the local GPU during the timed region."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    QUERY = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_id):
-        self.gpu = f"GPU-{gpu_id}" if not str(gpu_id).startswith("GPU-") else str(gpu_id)
+    def __init__(self, uuid: str):
+        self.uuid = uuid.lower().replace("gpu-", "")
         self.proc = None
         self.lines: list[str] = []
 
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self._t = threading.Thread(target=self._read, daemon=True)
             self._t.start()
@@ -134,7 +135,7 @@ class ClockSampler:
         rows = []
         for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 9 or parts[0].lower().replace("gpu-", "") != self.uuid:
                 continue
             try:
                 rows.append(dict(sm=float(parts[1]), max=float(parts[2]), power=float(parts[3]),
@@ -249,67 +250,83 @@ def run_ours(args, rank, world, local):
     lib = _lib.load()
     stream = torch.cuda.Stream(device=device)
 
-    def enqueue(events=None):
+    def enqueue(prep=True, gemm=True):
         s = _lib.stream_of(xs_dev[0])
         for j, ((m, k, n), x) in enumerate(zip(shapes, xs_dev)):
             layer, b = layers[(k, n)], bufs[j]
-            if events is not None:
-                events[j][0].record()
-            _lib.check(lib.convrot_prepare_i8(_lib.ptr(x), _lib.BF16, m, k, GROUP, _lib.ptr(b["codes"]),
-                                              _lib.ptr(b["xs"]), s), "prep")
-            if events is not None:
-                events[j][1].record()
-            _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(b["codes"]), _lib.ptr(layer.qweight), _lib.LAYOUT_KN,
-                                             _lib.ptr(b["xs"]), _lib.ptr(layer.scales), _lib.ptr(layer.bias),
-                                             _lib.ptr(b["out"]), _lib.BF16, m, n, k, s), "gemm")
-            if events is not None:
-                events[j][2].record()
+            if prep:
+                _lib.check(lib.convrot_prepare_i8(_lib.ptr(x), _lib.BF16, m, k, GROUP, _lib.ptr(b["codes"]),
+                                                  _lib.ptr(b["xs"]), s), "prep")
+            if gemm:
+                _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(b["codes"]), _lib.ptr(layer.qweight), _lib.LAYOUT_KN,
+                                                 _lib.ptr(b["xs"]), _lib.ptr(layer.scales), _lib.ptr(layer.bias),
+                                                 _lib.ptr(b["out"]), _lib.BF16, m, n, k, s), "gemm")
 
-    # warm-up (eager), then capture: a one-step graph for warm-up replays and a
-    # K-step graph with CUDA events around every kernel for the timed region
+    def capture(fn, reps=1):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(reps):
+                fn()
+        return g
+
+    def replay_ms(g, reps):
+        """Run ``g`` ``reps`` times on ``stream`` between two CUDA events."""
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    # warm-up (eager), then one graph per kind of pass: the full step (prep +
+    # GEMM for all 12 linears), the 12 GEMMs alone, the 12 preps alone
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
             enqueue()
     torch.cuda.synchronize()
-    warm_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(warm_graph, stream=stream):
-        enqueue()
-    events = [[[torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)] for _ in shapes]
-              for _ in range(args.steps)]
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for step in range(args.steps):
-            enqueue(events[step])
-    for _ in range(args.warmup):
-        warm_graph.replay()
-    torch.cuda.synchronize()
+    step_graph = capture(enqueue)
+    gemm_graph = capture(lambda: enqueue(prep=False))
+    prep_graph = capture(lambda: enqueue(gemm=False))
+    replay_ms(step_graph, args.warmup)
 
     # parity spot check of the benchmarked path against the public layer call
     ref = layers[KN_PAIRS[0]](xs_dev[0])
     assert torch.equal(ref, bufs[0]["out"]), "benchmark path and ConvRotLinear disagree"
 
-    # ---- timed region: K steps, one graph launch
+    # ---- timed region: K steps
     barrier(world)
     torch.cuda.synchronize()
-    with ClockSampler(torch.cuda.get_device_properties(device).uuid) as clocks:
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record(stream)
-        graph.replay()
-        t1.record(stream)
-        torch.cuda.synchronize()
+    with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
+        elapsed_ms = replay_ms(step_graph, args.steps)
     barrier(world)
-    elapsed_ms = t0.elapsed_time(t1)
     elapsed_ms = max_over_ranks(elapsed_ms, world)
-    prep_ms = [sum(events[st][j][0].elapsed_time(events[st][j][1]) for st in range(args.steps))
-               for j in range(len(shapes))]
-    gemm_ms = [sum(events[st][j][1].elapsed_time(events[st][j][2]) for st in range(args.steps))
-               for j in range(len(shapes))]
-    kernel_ms = (sum(prep_ms) + sum(gemm_ms)) / args.steps
+    # kernel-kind sweeps for the rooflines: same cold-operand order, events only at the ends
+    replay_ms(gemm_graph, 1)
+    gemm_sweep_ms = replay_ms(gemm_graph, args.steps) / args.steps
+    replay_ms(prep_graph, 1)
+    prep_sweep_ms = replay_ms(prep_graph, args.steps) / args.steps
+    # isolated per-shape GEMM times (each shape's GEMM replayed back to back)
+    per_shape = []
+    for j, (m, k, n) in enumerate(shapes):
+        b, layer = bufs[j], layers[(k, n)]
+
+        def one(j=j, m=m, k=k, n=n, b=b, layer=layer):
+            s = _lib.stream_of(xs_dev[0])
+            _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(b["codes"]), _lib.ptr(layer.qweight), _lib.LAYOUT_KN,
+                                             _lib.ptr(b["xs"]), _lib.ptr(layer.scales), _lib.ptr(layer.bias),
+                                             _lib.ptr(b["out"]), _lib.BF16, m, n, k, s), "gemm")
+
+        g1 = capture(one, reps=3)
+        replay_ms(g1, 1)
+        us = replay_ms(g1, 2) / 6 * 1e3
+        per_shape.append({"m": m, "k": k, "n": n, "gemm_us_isolated": round(us, 2),
+                          "gemm_tops_isolated": round(2 * m * k * n / (us * 1e-6) / 1e12, 1)})
+        del g1
     ops = total_ops(shapes)
     ms_per_step = elapsed_ms / args.steps
     value = world * ops * args.steps / (elapsed_ms * 1e-3) / 1e12
-
     # ---- dense bf16 cuBLAS on the same sweep (graph-captured, same L2 conditions)
     outs_dense = [torch.empty((m, n), dtype=torch.bfloat16, device=device) for (m, k, n) in shapes]
 
@@ -323,18 +340,9 @@ def run_ours(args, rank, world, local):
         for _ in range(max(1, args.warmup)):
             dense_step_addmm()
     torch.cuda.synchronize()
-    dgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(dgraph, stream=stream):
-        dense_step_addmm()
-    dgraph.replay()
-    torch.cuda.synchronize()
-    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    d0.record(stream)
-    for _ in range(args.steps):
-        dgraph.replay()
-    d1.record(stream)
-    torch.cuda.synchronize()
-    dense_ms = d0.elapsed_time(d1) / args.steps
+    dgraph = capture(dense_step_addmm)
+    replay_ms(dgraph, 1)
+    dense_ms = replay_ms(dgraph, args.steps) / args.steps
     dense_tflops = ops / (dense_ms * 1e-3) / 1e12
     del dgraph
 
@@ -342,11 +350,9 @@ def run_ours(args, rank, world, local):
     e2e = run_e2e(args, shapes, layers, xs_dev, device, world)
 
     # ---- rooflines
-    gemm_avg = [g / args.steps for g in gemm_ms]
-    prep_avg = [p / args.steps for p in prep_ms]
-    gemm_tops = sum(2 * m * k * n for m, k, n in shapes) / (sum(gemm_avg) * 1e-3) / 1e12
+    gemm_tops = ops / (gemm_sweep_ms * 1e-3) / 1e12
     prep_bytes = sum(2 * m * k + m * k + 4 * m for m, k, n in shapes)
-    prep_gbs = prep_bytes / (sum(prep_avg) * 1e-3) / 1e9
+    prep_gbs = prep_bytes / (prep_sweep_ms * 1e-3) / 1e9
     traffic = load_traffic()
     roofline = {
         "kernel": "w4a4_gemm_kernel (tcgen05 kind::i8)", "bound": "tensor",
@@ -354,22 +360,18 @@ def run_ours(args, rank, world, local):
         "frac": round(gemm_tops / int8_peak, 4),
         "peak_source": "dense int8 tensor ops/s of cuBLASLt (torch._int_mm 8192^3, burst) measured in this run; "
                        "MEASURED_PEAKS.json has no int8 entry; nominal 4500",
-        "ops_note": "int8 tensor ops (2 M N K per linear)",
+        "ops_note": "int8 tensor ops, 2 M N K per linear; time = the 12 GEMMs of one sweep in a CUDA graph, "
+                    "CUDA events on the launching stream, averaged over the K timed sweeps",
         "traffic": traffic.get("gemm_bytes_per_launch"),
     }
     roofline_prep = {
         "kernel": "prep_kernel (fused rotate + A4 quantize, int8 codes)", "bound": "hbm",
         "achieved": round(prep_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
         "frac": round(prep_gbs / peaks["hbm_gbs"], 4), "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peaks['source']})",
-        "bytes_note": "2MK (bf16 in) + MK (int8 codes) + 4M (scales) per launch",
+        "bytes_note": "2MK (bf16 in) + MK (int8 codes) + 4M (scales) per launch; time = the 12 preps of one sweep",
         "traffic": traffic.get("prep_bytes_per_launch"),
     }
     cpu = run_cpu_baseline(args, shapes, quick=True) if (rank == 0 and world == 1 and not args.no_cpu) else None
-    per_shape = [
-        {"m": m, "k": k, "n": n, "prep_us": round(p * 1e3, 2), "gemm_us": round(g * 1e3, 2),
-         "gemm_tops": round(2 * m * k * n / (g * 1e-3) / 1e12, 1)}
-        for (m, k, n), p, g in zip(shapes, prep_avg, gemm_avg)
-    ]
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -380,9 +382,9 @@ def run_ours(args, rank, world, local):
             "shapes_mkn": [list(s) for s in shapes], "group_size": GROUP, "weight_layout": "K x packed-N int4",
             "io_dtype": "bf16", "parallelism": f"replicas x{world} (batch data-parallel, no collective)",
             "l2": "per-step working set ~1.2 GB >> 126 MB L2; consecutive linears share no operand",
-            "timing": "CUDA graph of one step; kernel times from CUDA events inside the graph",
+            "timing": "CUDA graph of one step replayed K times between CUDA events on its stream",
         },
-        "kernel_ms_per_step": round(kernel_ms, 4),
+        "gemm_ms_per_sweep": round(gemm_sweep_ms, 4), "prep_ms_per_sweep": round(prep_sweep_ms, 4),
         "dense_bf16": {"value": round(dense_tflops, 1), "unit": "TFLOP/s", "ms_per_step": round(dense_ms, 4),
                        "impl": "torch.addmm bf16 (cuBLAS), same sweep, graph-captured"},
         "speedup_vs_dense_bf16": round(dense_ms / ms_per_step, 3),
@@ -394,7 +396,7 @@ def run_ours(args, rank, world, local):
         "per_shape": per_shape,
         "device_error": _lib.take_device_error(),
     }
-    del graph, warm_graph
+    del step_graph, gemm_graph, prep_graph
     return line
 
 

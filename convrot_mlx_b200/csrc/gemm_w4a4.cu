@@ -19,6 +19,8 @@
 // the main loop of tile i + 1.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -437,6 +439,339 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0 && bars->err) atomicCAS(&g_convrot_device_error, 0, bars->err);
 }
 
+// ===========================================================================
+// CTA-pair kernel (cta_group::2): pair tile 256 (M) x 256 (N), 256 K-bytes per
+// stage.  Each CTA of the pair owns 128 rows of A and 128 columns of B:
+//   warp 0    A producer: one 32 KB 3-D TMA box (two 128-byte K chunks) per
+//             stage into this CTA; completes on the pair leader's a_full
+//   warp 1    leader: MMA issuer (tcgen05.mma.cta_group::2, M = 256); both
+//             CTAs: TMEM allocation for the pair
+//   warp 2    packed-weight producer: one 16 KB TMA box per stage (this CTA's
+//             128 columns x 256 K), completing on this CTA's bp_full
+//   warps 3-6 transform: packed nibbles (shared) -> int8 x 16 in the
+//             128-byte-swizzled layout the tensor core reads, into a 2-slot
+//             ring; arrive on the leader's b8_ready
+//   warps 7-10 epilogue: this CTA's 128 accumulator rows x 256 columns
+// The leader's commits are multicast to both CTAs (stage release, int8-slot
+// release, accumulator ready); epilogue and transform warps of both CTAs
+// arrive on the leader's barriers through cluster addresses.  Per SM this
+// halves the weight bytes and the transform work of the one-CTA kernel for
+// the same tensor-core rate, and every operand arrives by TMA.
+// ===========================================================================
+namespace pair {
+
+constexpr int BM = 256;          // rows per pair tile (128 per CTA)
+constexpr int BN = 256;          // columns per pair tile (128 per CTA)
+constexpr int BK = 256;          // K bytes per stage
+constexpr int S = 3;             // TMA stages (A + packed B)
+constexpr int B8 = 2;            // int8 weight slots
+constexpr int kWarpA = 0, kWarpMma = 1, kWarpBp = 2, kWarpX0 = 3, kXWarps = 4, kWarpE0 = kWarpX0 + kXWarps,
+              kEWarps = 4;
+constexpr int kThreads = (kWarpE0 + kEWarps) * 32;  // 352
+constexpr int kXThreads = kXWarps * 32;
+constexpr int kABytes = 128 * BK;         // 32 KB per CTA per stage
+constexpr int kBpBytes = 128 * BK / 2;    // 16 KB
+constexpr int kB8Bytes = 128 * BK;        // 32 KB
+constexpr int kItems = kBpBytes / 16;     // 1024 transform items per stage
+constexpr int kItemsPerThread = kItems / kXThreads;  // 8
+constexpr int kEpiBytes = kEWarps * 2 * BN * 4;
+constexpr uint32_t kTmemCols = 2 * BN;
+
+struct alignas(8) Bars {
+  uint64_t a_full[S];
+  uint64_t bp_full[S];
+  uint64_t tma_empty[S];
+  uint64_t b8_ready[B8];
+  uint64_t b8_empty[B8];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int err;
+};
+
+constexpr size_t kSmemBytes = 1024 + S * (kABytes + kBpBytes) + B8 * kB8Bytes + kEpiBytes + sizeof(Bars);
+
+__device__ __noinline__ bool wait(uint64_t* bar, uint32_t parity, Bars* b, int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*reinterpret_cast<volatile int*>(&b->err)) return false;
+      if (globaltimer() - t0 > kTimeoutNs) {
+        atomicCAS(&b->err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+template <int LAYOUT, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                     const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                                   // S x 32 KB
+  uint8_t* sB8 = sA + S * kABytes;                      // B8 x 32 KB
+  uint8_t* sBp = sB8 + B8 * kB8Bytes;                   // S x 16 KB
+  float* epi = reinterpret_cast<float*>(sBp + S * kBpBytes);
+  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(epi) + kEpiBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const int pair_id = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+  const int k_stages = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars->a_full[s], 1);
+      mbar_init(&bars->bp_full[s], 1);
+      mbar_init(&bars->tma_empty[s], 1);
+    }
+    for (int s = 0; s < B8; ++s) {
+      mbar_init(&bars->b8_ready[s], 2 * kXWarps);
+      mbar_init(&bars->b8_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 2 * kEWarps);
+    }
+    mbar_init(&bars->mma_done, 1);
+    bars->err = 0;
+    fence_mbar_init();
+    prefetch_tensormap(&tmap_a);
+    prefetch_tensormap(&tmap_b);
+  }
+  if (warp == kWarpMma) {
+    tmem_alloc_pair(&bars->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialized before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == kWarpA) {
+    if (lane == 0) {
+      const uint32_t lead_a_full0 = mapa_shared(&bars->a_full[0], 0);
+      int g = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        const int m_row = (tile % p.m_tiles) * BM + 128 * rank;
+        for (int ks = 0; ks < k_stages; ++ks, ++g) {
+          const int slot = g % S;
+          if (!wait(&bars->tma_empty[slot], ((g / S) & 1) ^ 1, bars, 11)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&bars->a_full[slot], 2 * kABytes);
+          tma_load_3d_pair(sA + slot * kABytes, &tmap_a, lead_a_full0 + slot * 8, 0, m_row, 2 * ks);
+        }
+      }
+      // Copies complete on the leader's barrier, which this thread cannot poll
+      // in the peer CTA: after an error, give any copy still in flight 2 ms to
+      // land before the pair tears down.
+      if (!ok) {
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
+        }
+      }
+    }
+  } else if (warp == kWarpBp) {
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        const int n_col = (tile / p.m_tiles) * BN + 128 * rank;
+        for (int ks = 0; ks < k_stages; ++ks, ++g) {
+          const int slot = g % S;
+          if (!wait(&bars->tma_empty[slot], ((g / S) & 1) ^ 1, bars, 12)) { ok = false; break; }
+          mbar_arrive_expect_tx(&bars->bp_full[slot], kBpBytes);
+          if constexpr (LAYOUT == CONVROT_LAYOUT_NK)
+            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], ks * (BK / 2), n_col);
+          else
+            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], n_col / 2, ks * BK);
+        }
+      }
+      // a copy still in flight after an error lands before teardown
+      if (!ok) {
+        for (int j = 0; j < S && j < g; ++j) {
+          const int gg = g - 1 - j;
+          wait(&bars->bp_full[gg % S], (gg / S) & 1, bars, 12);
+        }
+      }
+    }
+  } else if (warp == kWarpMma) {
+    if (rank == 0 && lane == 0) {
+      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                             (static_cast<uint32_t>(LAYOUT == CONVROT_LAYOUT_KN) << 16) |
+                             (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB8);
+      int g = 0, local = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs, ++local) {
+        const int buf = local & 1;
+        if (!wait(&bars->acc_empty[buf], ((local >> 1) & 1) ^ 1, bars, 13)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int ks = 0; ks < k_stages; ++ks, ++g) {
+          const int slot = g % S, b8 = g % B8;
+          if (!wait(&bars->a_full[slot], (g / S) & 1, bars, 14)) { ok = false; break; }
+          if (!wait(&bars->b8_ready[b8], (g / B8) & 1, bars, 15)) { ok = false; break; }
+          tc_fence_after();
+          const int k_rem = p.K - ks * BK;
+          const int steps = k_rem >= BK ? BK / 32 : k_rem / 32;
+          const uint32_t a_addr = a_base + slot * kABytes;
+          const uint32_t b_addr = b_base + b8 * kB8Bytes;
+          for (int j = 0; j < steps; ++j) {
+            const uint32_t a_off = (j >> 2) * 16384 + (j & 3) * 32;
+            const uint64_t adesc = smem_desc(a_addr + a_off, 16, 1024, 2);
+            const uint64_t bdesc = LAYOUT == CONVROT_LAYOUT_NK ? smem_desc(b_addr + a_off, 16, 1024, 2)
+                                                               : smem_desc(b_addr + j * 4096, kB8Bytes, 1024, 2);
+            mma_i8_pair(d_tmem, adesc, bdesc, idesc, (ks | j) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair_multicast(&bars->tma_empty[slot], 0x3);
+          mma_commit_pair_multicast(&bars->b8_empty[b8], 0x3);
+        }
+        if (!ok) break;
+        mma_commit_pair_multicast(&bars->acc_full[buf], 0x3);
+      }
+      // every MMA issued above finishes before the pair's TMEM is released
+      mma_commit_pair_multicast(&bars->mma_done, 0x1);
+      wait(&bars->mma_done, 0, bars, 16);
+    }
+  } else if (warp < kWarpE0) {
+    // ---------------- transform ----------------
+    const int xt = threadIdx.x - kWarpX0 * 32;
+    const uint32_t lead_ready0 = mapa_shared(&bars->b8_ready[0], 0);
+    // per-item fixed geometry: packed source offset and the two int8 chunks
+    uint32_t src[kItemsPerThread], d0[kItemsPerThread], d1[kItemsPerThread];
+#pragma unroll
+    for (int i = 0; i < kItemsPerThread; ++i) {
+      const int item = i * kXThreads + xt;
+      if constexpr (LAYOUT == CONVROT_LAYOUT_NK) {
+        // packed row n (128 bytes = 256 K values), chunk c (32 K values) ->
+        // int8 K-chunk kc = c / 4, chunks 2j and 2j + 1 (j = c % 4) of row n.
+        // A quarter-warp takes rows 2p and 2p + 1 with opposite K-chunks: its
+        // loads cover both halves of the bank space and its stores land on
+        // chunk sets of opposite row parity -- eight distinct bank groups.
+        const int qw = item >> 3, l = item & 7, h = qw & 1;
+        const int n = 2 * (qw >> 1) + (l >> 2);
+        const int c = (l & 3) + 4 * ((l >> 2) ^ h);
+        const int kc = c >> 2, j = c & 3;
+        src[i] = n * 128 + c * 16;
+        const uint32_t row = kc * 16384 + n * 128;
+        d0[i] = row + (((2 * j) ^ (n & 7)) << 4);
+        d1[i] = row + (((2 * j + 1) ^ (n & 7)) << 4);
+      } else {
+        // packed row k (64 bytes = 128 N values), chunk c -> MN-major int8 row k
+        const int k = item >> 2, c = item & 3;
+        src[i] = k * 64 + c * 16;
+        const uint32_t row = (k >> 3) * 1024 + (k & 7) * 128;
+        d0[i] = row + (((2 * c) ^ (k & 7)) << 4);
+        d1[i] = row + (((2 * c + 1) ^ (k & 7)) << 4);
+      }
+    }
+    int g = 0;
+    bool ok = true;
+    for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+      for (int ks = 0; ks < k_stages; ++ks, ++g) {
+        const int slot = g % S, b8 = g % B8;
+        if (!wait(&bars->bp_full[slot], (g / S) & 1, bars, 17)) { ok = false; break; }
+        uint4 w[kItemsPerThread];
+        const uint8_t* bp = sBp + slot * kBpBytes;
+#pragma unroll
+        for (int i = 0; i < kItemsPerThread; ++i) w[i] = *reinterpret_cast<const uint4*>(bp + src[i]);
+        if (!wait(&bars->b8_empty[b8], ((g / B8) & 1) ^ 1, bars, 18)) { ok = false; break; }
+        const uint32_t dst = smem_u32(sB8 + b8 * kB8Bytes);
+#pragma unroll
+        for (int i = 0; i < kItemsPerThread; ++i) {
+          uint32_t o[8];
+          expand16(w[i], o);
+          sts128(dst + d0[i], o[0], o[1], o[2], o[3]);
+          sts128(dst + d1[i], o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(lead_ready0 + b8 * 8);
+      }
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int ew = warp & 3;
+    float* sws = epi + ew * 2 * BN;
+    float* sbias = sws + BN;
+    const uint32_t lead_empty0 = mapa_shared(&bars->acc_empty[0], 0);
+    int local = 0;
+    for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++local) {
+      const int buf = local & 1;
+      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      __syncwarp();
+      for (int j = lane; j < BN; j += 32) {
+        const int col = n_blk * BN + j;
+        sws[j] = col < p.N ? __ldg(p.wscales + col) : 0.0f;
+        sbias[j] = (col < p.N && p.bias) ? __ldg(p.bias + col) : 0.0f;
+      }
+      __syncwarp();
+      if (!wait(&bars->acc_full[buf], (local >> 1) & 1, bars, 19)) break;
+      tc_fence_after();
+      const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
+      const bool row_ok = m < p.M;
+      const float xs = row_ok ? __ldg(p.xscales + m) : 0.0f;
+      TOut* orow = static_cast<TOut*>(p.out) + static_cast<int64_t>(row_ok ? m : 0) * p.N;
+      const bool vec_store = (p.N % (16 / sizeof(TOut))) == 0;
+      const uint32_t t_row = tmem_base + ((ew * 32u) << 16) + buf * BN;
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n = n_blk * BN + c * 32;
+        if (n >= p.N) break;  // uniform across the warp
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
+          const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
+          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+          const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float dot = static_cast<float>(static_cast<int32_t>(r[j + u]) >> 4);
+            v[j + u] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), wv[u]), bv[u]);
+          }
+        }
+        if (!row_ok) continue;
+        if (vec_store && n + 32 <= p.N) {
+          store16(orow + n, v, 0);
+          store16(orow + n + 16, v, 16);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < p.N) orow[n + j] = cvt_out<TOut>(v[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(lead_empty0 + buf * 8);
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its partner may still touch its shared memory or TMEM
+  tc_fence_after();
+  if (warp == kWarpMma) {
+    __syncwarp();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && bars->err) atomicCAS(&g_convrot_device_error, 0, bars->err);
+}
+
+}  // namespace pair
+
 // ---------------------------------------------------------------------------
 // host side
 
@@ -466,6 +801,86 @@ int make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   CONVROT_REQUIRE(r == CUDA_SUCCESS, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return CONVROT_OK;
+}
+
+// Tiled uint8 tensor map of rank 2 or 3 (dims / strides in bytes, innermost first).
+int make_tmap_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
+                 const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  auto encode = get_encode_fn();
+  CONVROT_REQUIRE(encode != nullptr, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t d[3];
+  cuuint64_t st[2];
+  cuuint32_t b[3];
+  cuuint32_t es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), d, st, b, es,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CONVROT_REQUIRE(r == CUDA_SUCCESS, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return CONVROT_OK;
+}
+
+// The CTA-pair kernel needs K % 128 == 0 (A is read as 128-byte K chunks) and
+// a weight row stride that TMA can describe (K x packed-N: N % 32 == 0).
+bool pair_supported(int layout, int64_t n, int64_t k) {
+  return k % 128 == 0 && (layout == CONVROT_LAYOUT_NK || n % 32 == 0);
+}
+
+template <int LAYOUT, typename TOut>
+static int launch_pair(const int8_t* act, const Params& p0, cudaStream_t stream) {
+  Params p = p0;
+  p.m_tiles = (p.M + pair::BM - 1) / pair::BM;
+  p.n_tiles = (p.N + pair::BN - 1) / pair::BN;
+  CONVROT_REQUIRE(static_cast<int64_t>(p.m_tiles) * p.n_tiles < (1LL << 31), CONVROT_ERR_UNSUPPORTED,
+                  "too many output tiles");
+  CUtensorMap map_a, map_b;
+  {
+    // A viewed as (K / 128 chunks) x M rows x 128 bytes; one box = 2 chunks x 128 rows
+    const uint64_t dims[3] = {128, static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K / 128)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(p.K), 128};
+    const uint32_t box[3] = {128, 128, 2};
+    int rc = make_tmap_u8(&map_a, act, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc != CONVROT_OK) return rc;
+  }
+  {
+    int rc;
+    if (LAYOUT == CONVROT_LAYOUT_NK) {
+      const uint64_t dims[2] = {static_cast<uint64_t>(p.K / 2), static_cast<uint64_t>(p.N)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(p.K / 2)};
+      const uint32_t box[2] = {pair::BK / 2, 128};
+      rc = make_tmap_u8(&map_b, p.qweight, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    } else {
+      const uint64_t dims[2] = {static_cast<uint64_t>(p.N / 2), static_cast<uint64_t>(p.K)};
+      const uint64_t strides[1] = {static_cast<uint64_t>(p.N / 2)};
+      const uint32_t box[2] = {64, pair::BK};
+      rc = make_tmap_u8(&map_b, p.qweight, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    }
+    if (rc != CONVROT_OK) return rc;
+  }
+  auto kernel = pair::pair_gemm_kernel<LAYOUT, TOut>;
+  CONVROT_CUDA_CHECK(
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pair::kSmemBytes)));
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int max_pairs = device_sm_count() / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(pair::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pair::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, p));
+  return check_launch("w4a4 pair gemm");
 }
 
 template <int LAYOUT, typename TOut>
@@ -516,11 +931,27 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
   CONVROT_REQUIRE(static_cast<int64_t>(p.m_tiles) * p.n_tiles < (1LL << 31), CONVROT_ERR_UNSUPPORTED,
                   "too many output tiles");
   p.layout = layout;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const char* force = getenv("CONVROT_GEMM_KERNEL");  // "single" selects the one-CTA kernel (A/B testing)
+  const bool use_pair = w4a4::pair_supported(layout, n, k) && !(force && strcmp(force, "single") == 0);
+  if (use_pair) {
+    if (layout == CONVROT_LAYOUT_NK) {
+      switch (out_dtype) {
+        case CONVROT_BF16: return w4a4::launch_pair<CONVROT_LAYOUT_NK, __nv_bfloat16>(act, p, s);
+        case CONVROT_F16: return w4a4::launch_pair<CONVROT_LAYOUT_NK, __half>(act, p, s);
+        default: return w4a4::launch_pair<CONVROT_LAYOUT_NK, float>(act, p, s);
+      }
+    }
+    switch (out_dtype) {
+      case CONVROT_BF16: return w4a4::launch_pair<CONVROT_LAYOUT_KN, __nv_bfloat16>(act, p, s);
+      case CONVROT_F16: return w4a4::launch_pair<CONVROT_LAYOUT_KN, __half>(act, p, s);
+      default: return w4a4::launch_pair<CONVROT_LAYOUT_KN, float>(act, p, s);
+    }
+  }
   CUtensorMap map;
   int rc = w4a4::make_tmap_2d_u8(&map, act, static_cast<uint64_t>(k), static_cast<uint64_t>(m),
                                  static_cast<uint64_t>(k), w4a4::BK, w4a4::BM);
   if (rc != CONVROT_OK) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (layout == CONVROT_LAYOUT_NK) {
     switch (out_dtype) {
       case CONVROT_BF16: return w4a4::launch<CONVROT_LAYOUT_NK, __nv_bfloat16>(map, p, s);

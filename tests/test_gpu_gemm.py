@@ -19,6 +19,17 @@ from tests.gpu_util import assert_no_device_error, bf16_bits, cuda, host
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(params=["pair", "single"], autouse=True)
+def gemm_kernel(request, monkeypatch):
+    """Run every GEMM test on both tcgen05 kernels: the CTA-pair kernel (default
+    where it applies) and the one-CTA kernel (ragged K x packed-N weights)."""
+    if request.param == "single":
+        monkeypatch.setenv("CONVROT_GEMM_KERNEL", "single")
+    else:
+        monkeypatch.delenv("CONVROT_GEMM_KERNEL", raising=False)
+    return request.param
+
+
 def test_edges_nk_and_kn_match_reference():
     # reference tests/test_core.py:213-283 (37 x 64 x 46: M, N not multiples of anything)
     g = load_golden("edges_s2026082302")
@@ -74,7 +85,8 @@ def _random_case(m, n, k, seed):
 @pytest.mark.parametrize(
     "m,n,k",
     [(1, 2, 32), (37, 46, 64), (128, 256, 128), (129, 258, 160), (300, 520, 1024), (64, 1024, 1024),
-     (200, 34, 2688), (513, 1728, 3072), (17, 990, 96)],
+     (200, 34, 2688), (513, 1728, 3072), (17, 990, 96), (256, 256, 256), (255, 320, 384), (700, 1024, 2560),
+     (33, 64, 128)],
 )
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_random_shapes_both_layouts(m, n, k, out_dtype):

@@ -128,6 +128,20 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Cluster-scope acquire: for barriers that receive arrivals from the other
+// CTA of a pair.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -206,6 +220,16 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
 
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
+// Publishes this thread's earlier shared::cta writes to a cluster peer that
+// acquires the barrier: a release fence restricted to shared::cta (much
+// cheaper than a full cluster-scope release) followed by a relaxed remote
+// arrive.  The writer fences its generic stores for the async proxy first
+// when the tensor core is the reader.
+__device__ __forceinline__ void mbar_arrive_cluster_publish_smem(uint32_t bar_cluster_addr) {
+  asm volatile("fence.release.sync_restrict::shared::cta.cluster;" ::: "memory");
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync() {

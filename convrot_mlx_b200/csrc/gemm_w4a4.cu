@@ -492,11 +492,13 @@ struct alignas(8) Bars {
 
 constexpr size_t kSmemBytes = 1024 + S * (kABytes + kBpBytes) + B8 * kB8Bytes + kEpiBytes + sizeof(Bars);
 
+// Waits use cluster-scope acquire: most barriers of the pair kernel receive
+// arrivals from the other CTA.
 __device__ __noinline__ bool wait(uint64_t* bar, uint32_t parity, Bars* b, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((i & 255) == 0) {
       if (*reinterpret_cast<volatile int*>(&b->err)) return false;
       if (globaltimer() - t0 > kTimeoutNs) {
@@ -557,7 +559,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = bars->tmem_base;
 
   if (warp == kWarpA) {
-    if (lane == 0) {
+    // Lane s issues the copies of slot s: copies issued by one thread are
+    // served one after another, so one issuing lane per slot keeps S copies
+    // in flight.
+    if (lane < S) {
       const uint32_t lead_a_full0 = mapa_shared(&bars->a_full[0], 0);
       int g = 0;
       bool ok = true;
@@ -565,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m_row = (tile % p.m_tiles) * BM + 128 * rank;
         for (int ks = 0; ks < k_stages; ++ks, ++g) {
           const int slot = g % S;
+          if (slot != lane) continue;
           if (!wait(&bars->tma_empty[slot], ((g / S) & 1) ^ 1, bars, 11)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&bars->a_full[slot], 2 * kABytes);
           tma_load_3d_pair(sA + slot * kABytes, &tmap_a, lead_a_full0 + slot * 8, 0, m_row, 2 * ks);
@@ -580,13 +586,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == kWarpBp) {
-    if (lane == 0) {
+    if (lane < S) {  // one issuing lane per slot, as for A
       int g = 0;
       bool ok = true;
       for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
         const int n_col = (tile / p.m_tiles) * BN + 128 * rank;
         for (int ks = 0; ks < k_stages; ++ks, ++g) {
           const int slot = g % S;
+          if (slot != lane) continue;
           if (!wait(&bars->tma_empty[slot], ((g / S) & 1) ^ 1, bars, 12)) { ok = false; break; }
           mbar_arrive_expect_tx(&bars->bp_full[slot], kBpBytes);
           if constexpr (LAYOUT == CONVROT_LAYOUT_NK)
@@ -595,11 +602,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], n_col / 2, ks * BK);
         }
       }
-      // a copy still in flight after an error lands before teardown
+      // after an error, give a copy still in flight 2 ms to land before teardown
       if (!ok) {
-        for (int j = 0; j < S && j < g; ++j) {
-          const int gg = g - 1 - j;
-          wait(&bars->bp_full[gg % S], (gg / S) & 1, bars, 12);
+        const uint64_t t0 = globaltimer();
+        while (globaltimer() - t0 < 2000000ull) {
         }
       }
     }
@@ -693,9 +699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts128(dst + d0[i], o[0], o[1], o[2], o[3]);
           sts128(dst + d1[i], o[4], o[5], o[6], o[7]);
         }
-        fence_proxy_async_smem();
+        fence_proxy_async_smem();  // generic stores -> the pair MMA (async proxy)
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(lead_ready0 + b8 * 8);
+        if (lane == 0) mbar_arrive_cluster_publish_smem(lead_ready0 + b8 * 8);
       }
     }
   } else {

@@ -442,21 +442,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 // CTA-pair kernel (cta_group::2): pair tile 256 (M) x 256 (N), 256 K-bytes per
 // stage.  Each CTA of the pair owns 128 rows of A and 128 columns of B:
-//   warp 0    A producer: one 32 KB 3-D TMA box (two 128-byte K chunks) per
-//             stage into this CTA; completes on the pair leader's a_full
+//   warp 0    A producer: lane s owns slot s of the 3-slot ring and issues
+//             one 32 KB 3-D TMA box (two 128-byte K chunks) per stage into
+//             this CTA, completing on the pair leader's a_full.  Copies
+//             issued by one thread are served one after another, hence one
+//             issuing lane per slot.
 //   warp 1    leader: MMA issuer (tcgen05.mma.cta_group::2, M = 256); both
 //             CTAs: TMEM allocation for the pair
-//   warp 2    packed-weight producer: one 16 KB TMA box per stage (this CTA's
-//             128 columns x 256 K), completing on this CTA's bp_full
-//   warps 3-6 transform: packed nibbles (shared) -> int8 x 16 in the
+//   warp 2    packed-weight producer: lane s owns slot s; one 16 KB TMA box
+//             per stage (this CTA's 128 columns x 256 K) on this CTA's bp_full
+//   warps 3, 4, 6, 7  transform: packed nibbles (shared) -> int8 x 16 in the
 //             128-byte-swizzled layout the tensor core reads, into a 2-slot
-//             ring; arrive on the leader's b8_ready
-//   warps 7-10 epilogue: this CTA's 128 accumulator rows x 256 columns
+//             ring.  The leader's warps arrive on its b8_ready; the peer's
+//             warps each bulk-copy a 16-byte token into the leader, completing
+//             bytes on that barrier (a copy-engine signal).
+//   warp 5    idle, so that the MMA issuer has its scheduler to itself
+//   warps 8-11 epilogue: this CTA's 128 accumulator rows x 256 columns
 // The leader's commits are multicast to both CTAs (stage release, int8-slot
-// release, accumulator ready); epilogue and transform warps of both CTAs
-// arrive on the leader's barriers through cluster addresses.  Per SM this
-// halves the weight bytes and the transform work of the one-CTA kernel for
-// the same tensor-core rate, and every operand arrives by TMA.
+// release, accumulator ready); the peer's epilogue warps arrive on the
+// leader's acc_empty through cluster addresses.  Per SM this halves the
+// weight bytes and the transform work of the one-CTA kernel for the same
+// tensor-core rate, and every operand arrives by TMA.
 // ===========================================================================
 namespace pair {
 
@@ -465,9 +471,13 @@ constexpr int BN = 256;          // columns per pair tile (128 per CTA)
 constexpr int BK = 256;          // K bytes per stage
 constexpr int S = 3;             // TMA stages (A + packed B)
 constexpr int B8 = 2;            // int8 weight slots
-constexpr int kWarpA = 0, kWarpMma = 1, kWarpBp = 2, kWarpX0 = 3, kXWarps = 4, kWarpE0 = kWarpX0 + kXWarps,
+// Warp w runs on scheduler w % 4.  The MMA issuer (warp 1) shares its
+// scheduler with no transform warp: warp 5 idles, the transform warps are
+// 3, 4, 6 and 7, the epilogue warps 8-11 (warp w reads TMEM lanes
+// 32 * (w % 4) .. + 31).
+constexpr int kWarpA = 0, kWarpMma = 1, kWarpBp = 2, kWarpX0 = 3, kXWarps = 4, kWarpIdle = 5, kWarpE0 = 8,
               kEWarps = 4;
-constexpr int kThreads = (kWarpE0 + kEWarps) * 32;  // 352
+constexpr int kThreads = (kWarpE0 + kEWarps) * 32;  // 384
 constexpr int kXThreads = kXWarps * 32;
 constexpr int kABytes = 128 * BK;         // 32 KB per CTA per stage
 constexpr int kBpBytes = 128 * BK / 2;    // 16 KB
@@ -477,7 +487,12 @@ constexpr int kItemsPerThread = kItems / kXThreads;  // 8
 constexpr int kEpiBytes = kEWarps * 2 * BN * 4;
 constexpr uint32_t kTmemCols = 2 * BN;
 
-struct alignas(8) Bars {
+struct alignas(16) Bars {
+  // The peer's transform warps signal the leader's b8_ready by copying a
+  // 16-byte token each into tok (a bulk copy completing bytes on b8_ready):
+  // copy-engine signals reach the leader much sooner than remote arrives.
+  uint8_t tok[B8][kXWarps][16];
+  uint8_t tok_src[16];
   uint64_t a_full[S];
   uint64_t bp_full[S];
   uint64_t tma_empty[S];
@@ -509,6 +524,15 @@ __device__ __noinline__ bool wait(uint64_t* bar, uint32_t parity, Bars* b, int c
   }
 }
 
+__device__ __forceinline__ void settle_after_error(bool ok) {
+  // after an error, give an asynchronous copy still in flight 2 ms to land
+  if (!ok) {
+    const uint64_t t0 = globaltimer();
+    while (globaltimer() - t0 < 2000000ull) {
+    }
+  }
+}
+
 template <int LAYOUT, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
@@ -536,7 +560,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bars->tma_empty[s], 1);
     }
     for (int s = 0; s < B8; ++s) {
-      mbar_init(&bars->b8_ready[s], 2 * kXWarps);
+      mbar_init(&bars->b8_ready[s], kXWarps);  // the leader's warps; the peer's arrive as bytes
       mbar_init(&bars->b8_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -648,10 +672,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit_pair_multicast(&bars->mma_done, 0x1);
       wait(&bars->mma_done, 0, bars, 16);
     }
+  } else if (warp == kWarpIdle) {
   } else if (warp < kWarpE0) {
     // ---------------- transform ----------------
-    const int xt = threadIdx.x - kWarpX0 * 32;
+    const int xw = warp < kWarpIdle ? warp - kWarpX0 : warp - kWarpX0 - 1;  // 0..3
+    const int xt = xw * 32 + lane;
     const uint32_t lead_ready0 = mapa_shared(&bars->b8_ready[0], 0);
+    const uint32_t lead_tok0 = mapa_shared(&bars->tok[0][0][0], 0);
     // per-item fixed geometry: packed source offset and the two int8 chunks
     uint32_t src[kItemsPerThread], d0[kItemsPerThread], d1[kItemsPerThread];
 #pragma unroll
@@ -701,9 +728,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         fence_proxy_async_smem();  // generic stores -> the pair MMA (async proxy)
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster_publish_smem(lead_ready0 + b8 * 8);
+        if (lane == 0) {
+          if (rank == 0) {
+            // the leader's warp 0 also announces the peer's token bytes
+            if (xw == 0) mbar_arrive_expect_tx(&bars->b8_ready[b8], kXWarps * 16);
+            else mbar_arrive(&bars->b8_ready[b8]);
+          } else {
+            bulk_copy_to_peer(lead_tok0 + (b8 * kXWarps + xw) * 16, bars->tok_src, 16, lead_ready0 + b8 * 8);
+          }
+        }
       }
     }
+    if (lane == 0) settle_after_error(ok);  // a token copy may still be in flight
   } else {
     // ---------------- epilogue ----------------
     const int ew = warp & 3;

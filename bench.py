@@ -299,7 +299,16 @@ def run_ours(args, rank, world, local):
     barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
+        # nvidia-smi samples every 200 ms while the timed region lasts a few ms:
+        # untimed replays keep the GPU under the same load for ~0.6 s before
+        # and ~0.4 s after it, and the samples of that window are reported
+        load_until = time.perf_counter() + 0.6
+        while time.perf_counter() < load_until:
+            replay_ms(step_graph, 8)
         elapsed_ms = replay_ms(step_graph, args.steps)
+        load_until = time.perf_counter() + 0.4
+        while time.perf_counter() < load_until:
+            replay_ms(step_graph, 8)
     barrier(world)
     elapsed_ms = max_over_ranks(elapsed_ms, world)
     # kernel-kind sweeps for the rooflines: same cold-operand order, events only at the ends
@@ -354,12 +363,15 @@ def run_ours(args, rank, world, local):
     prep_bytes = sum(2 * m * k + m * k + 4 * m for m, k, n in shapes)
     prep_gbs = prep_bytes / (prep_sweep_ms * 1e-3) / 1e9
     traffic = load_traffic()
+    bf16_x2 = 2 * peaks["bf16_tflops"]
     roofline = {
-        "kernel": "w4a4_gemm_kernel (tcgen05 kind::i8)", "bound": "tensor",
+        "kernel": "pair_gemm_kernel (tcgen05.mma.cta_group::2 kind::i8, 256x256 pair tiles)", "bound": "tensor",
         "achieved": round(gemm_tops, 1), "peak": round(int8_peak, 1), "unit": "TFLOP/s",
         "frac": round(gemm_tops / int8_peak, 4),
         "peak_source": "dense int8 tensor ops/s of cuBLASLt (torch._int_mm 8192^3, burst) measured in this run; "
                        "MEASURED_PEAKS.json has no int8 entry; nominal 4500",
+        "frac_of_2x_measured_bf16": round(gemm_tops / bf16_x2, 4),
+        "bf16_x2_peak": round(bf16_x2, 1),
         "ops_note": "int8 tensor ops, 2 M N K per linear; time = the 12 GEMMs of one sweep in a CUDA graph, "
                     "CUDA events on the launching stream, averaged over the K timed sweeps",
         "traffic": traffic.get("gemm_bytes_per_launch"),
@@ -391,7 +403,8 @@ def run_ours(args, rank, world, local):
         "roofline": roofline, "roofline_prep": roofline_prep,
         "e2e": e2e,
         "gpu_launches": 2 * len(shapes) * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": dict(clocks.summary(), window="nvidia-smi 200 ms samples over ~1 s of step replays enclosing "
+                                                  "the timed region"),
         "cpu_baseline": cpu,
         "per_shape": per_shape,
         "device_error": _lib.take_device_error(),
@@ -526,6 +539,35 @@ def run_reference(args, rank, world):
     }
 
 
+def run_case(args):
+    """One kernel on one shape, launched ``--case-launches`` times on the
+    default stream (eager), for profilers: ``--case gemm`` runs the W4A4 GEMM
+    (K x packed-N weights), ``--case prep`` the fused rotate + A4 quantize."""
+
+    import convrot_mlx_b200 as cr
+    from convrot_mlx_b200 import _lib
+
+    device = torch.device("cuda", 0)
+    m, k, n = args.m, args.k, args.n
+    x = make_activation(m, k, SEED, device)
+    if args.case == "prep":
+        for _ in range(args.case_launches):
+            cr.metal_fused_prepare_convrot_activation_i8(x, args.group)
+    else:
+        layer, _, _ = make_linear(k, n, SEED, device)
+        codes, xs = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+        lib = _lib.load()
+        for _ in range(args.case_launches):
+            _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(codes), _lib.ptr(layer.qweight), _lib.LAYOUT_KN, _lib.ptr(xs),
+                                             _lib.ptr(layer.scales), _lib.ptr(layer.bias), _lib.ptr(out), _lib.BF16,
+                                             m, n, k, _lib.stream_of(x)), "gemm")
+    torch.cuda.synchronize()
+    err = _lib.take_device_error()
+    print(json.dumps({"case": args.case, "m": m, "k": k, "n": n, "launches": args.case_launches, "device_error": err}))
+    return 1 if err else 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -533,7 +575,15 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--case", choices=("gemm", "prep"), help="run one kernel on one shape (for profilers) and exit")
+    ap.add_argument("--m", type=int, default=4096)
+    ap.add_argument("--k", type=int, default=3072)
+    ap.add_argument("--n", type=int, default=12288)
+    ap.add_argument("--group", type=int, default=GROUP)
+    ap.add_argument("--case-launches", type=int, default=3)
     args = ap.parse_args(argv)
+    if args.case:
+        return run_case(args)
     if args.warmup < 1:
         args.warmup = 1
     if args.impl == "reference":

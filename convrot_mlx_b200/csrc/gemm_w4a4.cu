@@ -29,6 +29,18 @@ namespace convrot {
 
 __device__ int g_convrot_device_error = 0;
 
+int* device_error_word() {
+  static int* words[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (words[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_convrot_device_error) != cudaSuccess) return nullptr;
+    words[dev] = static_cast<int*>(p);
+  }
+  return words[dev];
+}
+
 namespace w4a4 {
 
 constexpr int BM = 128;
@@ -74,12 +86,6 @@ struct Params {
   int m_tiles, n_tiles, k_blocks;
   int layout;
 };
-
-__device__ __forceinline__ uint64_t globaltimer() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
 
 // Wait for the phase of `bar` with parity `parity` to complete, for at most
 // kTimeoutNs.  On time-out record the error in shared memory and return false.

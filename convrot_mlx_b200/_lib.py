@@ -40,6 +40,7 @@ SIGNATURES: dict[str, tuple] = {
     "convrot_pack_int4": (_I, [_P, _I64, _P, _P]),
     "convrot_repack_int4_transpose": (_I, [_P, _I64, _I64, _P, _P]),
     "convrot_w4a4_gemm": (_I, [_P, _P, _I, _P, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
+    "convrot_w4a16_gemm": (_I, [_P, _I, _P, _I, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "convrot_take_device_error": (_I, [ctypes.POINTER(_I)]),
 }
 

@@ -363,22 +363,34 @@ def mpp_w4a16_matmul(activations, qweight, wscales, bias, *, output_dtype) -> to
 
 def _gemm_w4a16(act, qweight, layout, wscales, bias, output_dtype, m, n, k) -> torch.Tensor:
     lib = _lib.load()
-    if not hasattr(lib, "convrot_w4a16_gemm"):
-        raise NotImplementedError("the W4A16 tcgen05 GEMM is not part of this build yet")
     _require_cuda(act, qweight, wscales, bias)
     a = act.contiguous()
     w = qweight.contiguous()
     ws = _f32_vec(wscales)
     b = None if bias is None else _f32_vec(bias)
-    out = torch.empty((m, n), dtype=output_dtype, device=a.device)
+    # The tcgen05 kernel reads 64-value K chunks and, for K x packed-N
+    # weights, 16-byte weight rows (N % 32 == 0).  Ragged shapes are padded
+    # with zeros on the device (zero codes add nothing to a dot) and the
+    # output is cut back to N.
+    kp = -(-k // 64) * 64
+    np_ = -(-n // 32) * 32 if layout == _lib.LAYOUT_KN else n
+    if kp != k:
+        a = torch.nn.functional.pad(a, (0, kp - k))
+        w = torch.nn.functional.pad(w, (0, (kp - k) // 2)) if layout == _lib.LAYOUT_NK else \
+            torch.nn.functional.pad(w, (0, 0, 0, kp - k))
+    if np_ != n:
+        w = torch.nn.functional.pad(w, (0, (np_ - n) // 2))
+        ws = torch.nn.functional.pad(ws, (0, np_ - n))
+        b = None if b is None else torch.nn.functional.pad(b, (0, np_ - n))
+    out = torch.empty((m, np_), dtype=output_dtype, device=a.device)
     _lib.check(
         lib.convrot_w4a16_gemm(
             _lib.ptr(a), _dtype_code(a.dtype), _lib.ptr(w), layout, _lib.ptr(ws), _lib.ptr(b), _lib.ptr(out),
-            _dtype_code(output_dtype), m, n, k, _lib.stream_of(a),
+            _dtype_code(output_dtype), m, np_, kp, _lib.stream_of(a),
         ),
         "W4A16 GEMM",
     )
-    return out
+    return out if np_ == n else out[:, :n].contiguous()
 
 
 def _validate_packed_nk(qact, qweight, what="packed W4A4"):

@@ -336,6 +336,16 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on the mbarrier at the same shared-memory offset in every CTA of
 // `cta_mask` once all pair MMAs issued before by this thread are complete.
 __device__ __forceinline__ void mma_commit_pair_multicast(uint64_t* bar, uint16_t cta_mask) {

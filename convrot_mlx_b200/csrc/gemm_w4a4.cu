@@ -493,6 +493,15 @@ constexpr int kItemsPerThread = kItems / kXThreads;  // 8
 constexpr int kEpiBytes = kEWarps * 2 * BN * 4;
 constexpr uint32_t kTmemCols = 2 * BN;
 
+// Operand kinds.  KIND_I8: A4 int8 codes x nibbles expanded to int8 x 16
+// (kind::i8, int32 accumulate; W4A4).  KIND_BF16 / KIND_F16: rotated 16-bit
+// activations x nibbles expanded to exact 16-bit integers (kind::f16, fp32
+// accumulate; W4A16).  A stage is 256 bytes of A's K extent either way.
+constexpr int KIND_I8 = 0, KIND_BF16 = 1, KIND_F16 = 2;
+template <int KIND> constexpr int kKStage = KIND == KIND_I8 ? 256 : 128;  // K per stage
+template <int KIND> constexpr int kKStep = KIND == KIND_I8 ? 32 : 16;     // K per MMA
+template <int KIND> constexpr int kBpStage = 128 * kKStage<KIND> / 2;     // packed bytes per CTA per stage
+
 struct alignas(16) Bars {
   // The peer's transform warps signal the leader's b8_ready by copying a
   // 16-byte token each into tok (a bulk copy completing bytes on b8_ready):
@@ -539,7 +548,33 @@ __device__ __forceinline__ void settle_after_error(bool ok) {
   }
 }
 
-template <int LAYOUT, typename TOut>
+// Four packed words (32 nibbles) -> 32 exact 16-bit integers in 4 chunks of
+// 16 bytes.  The biased nibble u = nibble ^ 8 goes into the low mantissa bits
+// of 128.0 (bf16, 0x4300) or 1024.0 (fp16, 0x6400), whose ulp is 1; one
+// packed subtraction of 136 / 1032 then leaves the signed value exactly.
+template <int KIND>
+__device__ __forceinline__ void expand16_to_16bit(const uint4 w, uint32_t (&o)[16]) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+  constexpr uint32_t kBase = KIND == KIND_BF16 ? 0x43004300u : 0x64006400u;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t y = in[q] ^ 0x88888888u;
+    const uint32_t lo = y & 0x0F0F0F0Fu, hi = (y >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const uint32_t v = (__byte_perm(lo, hi, t | ((4 + t) << 8)) & 0x00FF00FFu) | kBase;
+      if constexpr (KIND == KIND_BF16) {
+        const __nv_bfloat162 r = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v), __float2bfloat162_rn(136.0f));
+        o[4 * q + t] = *reinterpret_cast<const uint32_t*>(&r);
+      } else {
+        const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&v), __float2half2_rn(1032.0f));
+        o[4 * q + t] = *reinterpret_cast<const uint32_t*>(&r);
+      }
+    }
+  }
+}
+
+template <int LAYOUT, typename TOut, int KIND = KIND_I8>
 __global__ void __launch_bounds__(kThreads, 1)
     pair_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const Params p) {
@@ -557,7 +592,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair_id = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int num_tiles = p.m_tiles * p.n_tiles;
-  const int k_stages = (p.K + BK - 1) / BK;
+  constexpr int KS = kKStage<KIND>;
+  const int k_stages = (p.K + KS - 1) / KS;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -625,11 +661,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int slot = g % S;
           if (slot != lane) continue;
           if (!wait(&bars->tma_empty[slot], ((g / S) & 1) ^ 1, bars, 12)) { ok = false; break; }
-          mbar_arrive_expect_tx(&bars->bp_full[slot], kBpBytes);
+          mbar_arrive_expect_tx(&bars->bp_full[slot], kBpStage<KIND>);
           if constexpr (LAYOUT == CONVROT_LAYOUT_NK)
-            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], ks * (BK / 2), n_col);
+            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], ks * (KS / 2), n_col);
           else
-            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], n_col / 2, ks * BK);
+            tma_load_2d(sBp + slot * kBpBytes, &tmap_b, &bars->bp_full[slot], n_col / 2, ks * KS);
         }
       }
       // after an error, give a copy still in flight 2 ms to land before teardown
@@ -641,8 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma) {
     if (rank == 0 && lane == 0) {
-      const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) |
-                             (static_cast<uint32_t>(LAYOUT == CONVROT_LAYOUT_KN) << 16) |
+      // D format (s32 / f32), A and B formats (s8 / bf16 / f16), B major, N, M
+      constexpr uint32_t kFormats = KIND == KIND_I8     ? (2u << 4) | (1u << 7) | (1u << 10)
+                                    : KIND == KIND_BF16 ? (1u << 4) | (1u << 7) | (1u << 10)
+                                                        : (1u << 4);
+      const uint32_t idesc = kFormats | (static_cast<uint32_t>(LAYOUT == CONVROT_LAYOUT_KN) << 16) |
                              (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
       const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB8);
       int g = 0, local = 0;
@@ -657,16 +696,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wait(&bars->a_full[slot], (g / S) & 1, bars, 14)) { ok = false; break; }
           if (!wait(&bars->b8_ready[b8], (g / B8) & 1, bars, 15)) { ok = false; break; }
           tc_fence_after();
-          const int k_rem = p.K - ks * BK;
-          const int steps = k_rem >= BK ? BK / 32 : k_rem / 32;
+          const int k_rem = p.K - ks * KS;
+          const int steps = k_rem >= KS ? KS / kKStep<KIND> : k_rem / kKStep<KIND>;
           const uint32_t a_addr = a_base + slot * kABytes;
           const uint32_t b_addr = b_base + b8 * kB8Bytes;
           for (int j = 0; j < steps; ++j) {
             const uint32_t a_off = (j >> 2) * 16384 + (j & 3) * 32;
             const uint64_t adesc = smem_desc(a_addr + a_off, 16, 1024, 2);
-            const uint64_t bdesc = LAYOUT == CONVROT_LAYOUT_NK ? smem_desc(b_addr + a_off, 16, 1024, 2)
-                                                               : smem_desc(b_addr + j * 4096, kB8Bytes, 1024, 2);
-            mma_i8_pair(d_tmem, adesc, bdesc, idesc, (ks | j) != 0 ? 1u : 0u);
+            // B: K-major (NK) like A; MN-major (KN): K step = 32 (int8) or 16
+            // (16-bit) rows of 128 bytes; 16-bit tiles hold two 64-column
+            // atoms 16 KB apart (the leading byte offset)
+            const uint64_t bdesc = LAYOUT == CONVROT_LAYOUT_NK
+                                       ? smem_desc(b_addr + a_off, 16, 1024, 2)
+                                       : (KIND == KIND_I8 ? smem_desc(b_addr + j * 4096, kB8Bytes, 1024, 2)
+                                                          : smem_desc(b_addr + j * 2048, 16384, 1024, 2));
+            if constexpr (KIND == KIND_I8)
+              mma_i8_pair(d_tmem, adesc, bdesc, idesc, (ks | j) != 0 ? 1u : 0u);
+            else
+              mma_f16_pair(d_tmem, adesc, bdesc, idesc, (ks | j) != 0 ? 1u : 0u);
           }
           mma_commit_pair_multicast(&bars->tma_empty[slot], 0x3);
           mma_commit_pair_multicast(&bars->b8_empty[b8], 0x3);
@@ -685,6 +732,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int xt = xw * 32 + lane;
     const uint32_t lead_ready0 = mapa_shared(&bars->b8_ready[0], 0);
     const uint32_t lead_tok0 = mapa_shared(&bars->tok[0][0][0], 0);
+    auto publish = [&](int b8) {
+      fence_proxy_async_smem();  // generic stores -> the pair MMA (async proxy)
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) {
+          // the leader's warp 0 also announces the peer's token bytes
+          if (xw == 0) mbar_arrive_expect_tx(&bars->b8_ready[b8], kXWarps * 16);
+          else mbar_arrive(&bars->b8_ready[b8]);
+        } else {
+          bulk_copy_to_peer(lead_tok0 + (b8 * kXWarps + xw) * 16, bars->tok_src, 16, lead_ready0 + b8 * 8);
+        }
+      }
+    };
+    bool ok = true;
+    if constexpr (KIND == KIND_I8) {
     // per-item fixed geometry: packed source offset and the two int8 chunks
     uint32_t src[kItemsPerThread], d0[kItemsPerThread], d1[kItemsPerThread];
 #pragma unroll
@@ -714,7 +776,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     int g = 0;
-    bool ok = true;
     for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
       for (int ks = 0; ks < k_stages; ++ks, ++g) {
         const int slot = g % S, b8 = g % B8;
@@ -732,16 +793,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           sts128(dst + d0[i], o[0], o[1], o[2], o[3]);
           sts128(dst + d1[i], o[4], o[5], o[6], o[7]);
         }
-        fence_proxy_async_smem();  // generic stores -> the pair MMA (async proxy)
-        __syncwarp();
-        if (lane == 0) {
-          if (rank == 0) {
-            // the leader's warp 0 also announces the peer's token bytes
-            if (xw == 0) mbar_arrive_expect_tx(&bars->b8_ready[b8], kXWarps * 16);
-            else mbar_arrive(&bars->b8_ready[b8]);
-          } else {
-            bulk_copy_to_peer(lead_tok0 + (b8 * kXWarps + xw) * 16, bars->tok_src, 16, lead_ready0 + b8 * 8);
+        publish(b8);
+      }
+    }
+    } else {
+      // W4A16: packed row r (64 bytes = 128 values), 16-byte chunk c (32
+      // values) -> 32 16-bit values in 64-value atom c / 2, 16-byte chunks
+      // 4 (c % 2) .. + 3 of row r (row r at (r / 8) * 1024 + (r % 8) * 128 of
+      // the atom, chunk index XOR r % 8).  NK: r = column n, K-major atoms of
+      // 64 K.  KN: r = k, MN-major atoms of 64 columns.  A quarter-warp takes
+      // rows 4q .. 4q + 3 with c in {0, 1} or {2, 3}: each of its stores hits
+      // 8 distinct chunk positions.
+      constexpr int kIt = kBpStage<KIND> / 16 / kXThreads;  // 4
+      uint32_t src[kIt], rowoff[kIt], cbase[kIt], rsw[kIt];
+#pragma unroll
+      for (int i = 0; i < kIt; ++i) {
+        const int item = i * kXThreads + xt;
+        const int qw = item >> 3, l = item & 7;
+        const int r = 4 * (qw >> 1) + (l >> 1), c = ((qw & 1) << 1) | (l & 1);
+        src[i] = r * 64 + c * 16;
+        rowoff[i] = (c >> 1) * 16384 + (r >> 3) * 1024 + (r & 7) * 128;
+        cbase[i] = (c & 1) * 4;
+        rsw[i] = r & 7;
+      }
+      int g = 0;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        for (int ks = 0; ks < k_stages; ++ks, ++g) {
+          const int slot = g % S, b8 = g % B8;
+          if (!wait(&bars->bp_full[slot], (g / S) & 1, bars, 17)) { ok = false; break; }
+          uint4 w[kIt];
+          const uint8_t* bp = sBp + slot * kBpBytes;
+#pragma unroll
+          for (int i = 0; i < kIt; ++i) w[i] = *reinterpret_cast<const uint4*>(bp + src[i]);
+          if (!wait(&bars->b8_empty[b8], ((g / B8) & 1) ^ 1, bars, 18)) { ok = false; break; }
+          const uint32_t dst = smem_u32(sB8 + b8 * kB8Bytes);
+#pragma unroll
+          for (int i = 0; i < kIt; ++i) {
+            uint32_t o[16];
+            expand16_to_16bit<KIND>(w[i], o);
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              sts128(dst + rowoff[i] + (((cbase[i] + q) ^ rsw[i]) << 4), o[4 * q], o[4 * q + 1], o[4 * q + 2],
+                     o[4 * q + 3]);
           }
+          publish(b8);
         }
       }
     }
@@ -767,7 +862,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
       const bool row_ok = m < p.M;
-      const float xs = row_ok ? __ldg(p.xscales + m) : 0.0f;
+      const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
       TOut* orow = static_cast<TOut*>(p.out) + static_cast<int64_t>(row_ok ? m : 0) * p.N;
       const bool vec_store = (p.N % (16 / sizeof(TOut))) == 0;
       const uint32_t t_row = tmem_base + ((ew * 32u) << 16) + buf * BN;
@@ -787,8 +882,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const float dot = static_cast<float>(static_cast<int32_t>(r[j + u]) >> 4);
-            v[j + u] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), wv[u]), bv[u]);
+            if constexpr (KIND == KIND_I8) {
+              // core.py:932-936: fl(fl(fl(dot) * xs) * ws) + bias
+              const float dot = static_cast<float>(static_cast<int32_t>(r[j + u]) >> 4);
+              v[j + u] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), wv[u]), bv[u]);
+            } else {
+              // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
+              v[j + u] = __fadd_rn(__fmul_rn(__uint_as_float(r[j + u]), wv[u]), bv[u]);
+            }
           }
         }
         if (!row_ok) continue;
@@ -853,7 +954,8 @@ int make_tmap_2d_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 
 // Tiled uint8 tensor map of rank 2 or 3 (dims / strides in bytes, innermost first).
 int make_tmap_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* dims, const uint64_t* strides,
-                 const uint32_t* box, CUtensorMapSwizzle swizzle) {
+                 const uint32_t* box, CUtensorMapSwizzle swizzle,
+                 CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_UINT8) {
   auto encode = get_encode_fn();
   CONVROT_REQUIRE(encode != nullptr, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   cuuint64_t d[3];
@@ -865,9 +967,8 @@ int make_tmap_u8(CUtensorMap* map, const void* base, int rank, const uint64_t* d
     b[i] = box[i];
   }
   for (int i = 0; i + 1 < rank; ++i) st[i] = strides[i];
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), d, st, b, es,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode(map, dtype, rank, const_cast<void*>(base), d, st, b, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   CONVROT_REQUIRE(r == CUDA_SUCCESS, CONVROT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return CONVROT_OK;
 }
@@ -878,20 +979,24 @@ bool pair_supported(int layout, int64_t n, int64_t k) {
   return k % 128 == 0 && (layout == CONVROT_LAYOUT_NK || n % 32 == 0);
 }
 
-template <int LAYOUT, typename TOut>
-static int launch_pair(const int8_t* act, const Params& p0, cudaStream_t stream) {
+template <int LAYOUT, typename TOut, int KIND = pair::KIND_I8>
+static int launch_pair(const void* act, const Params& p0, cudaStream_t stream) {
   Params p = p0;
   p.m_tiles = (p.M + pair::BM - 1) / pair::BM;
   p.n_tiles = (p.N + pair::BN - 1) / pair::BN;
   CONVROT_REQUIRE(static_cast<int64_t>(p.m_tiles) * p.n_tiles < (1LL << 31), CONVROT_ERR_UNSUPPORTED,
                   "too many output tiles");
+  constexpr bool k16 = KIND != pair::KIND_I8;
+  constexpr int KS = pair::kKStage<KIND>;
   CUtensorMap map_a, map_b;
   {
-    // A viewed as (K / 128 chunks) x M rows x 128 bytes; one box = 2 chunks x 128 rows
-    const uint64_t dims[3] = {128, static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K / 128)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(p.K), 128};
-    const uint32_t box[3] = {128, 128, 2};
-    int rc = make_tmap_u8(&map_a, act, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    // A viewed as (K / chunk) x M rows x one 128-byte chunk; one box = 2 chunks x 128 rows
+    const uint64_t chunk = k16 ? 64 : 128;  // elements per 128 bytes
+    const uint64_t dims[3] = {chunk, static_cast<uint64_t>(p.M), static_cast<uint64_t>(p.K) / chunk};
+    const uint64_t strides[2] = {static_cast<uint64_t>(p.K) * (k16 ? 2 : 1), 128};
+    const uint32_t box[3] = {static_cast<uint32_t>(chunk), 128, 2};
+    int rc = make_tmap_u8(&map_a, act, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
+                          k16 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8);
     if (rc != CONVROT_OK) return rc;
   }
   {
@@ -899,17 +1004,17 @@ static int launch_pair(const int8_t* act, const Params& p0, cudaStream_t stream)
     if (LAYOUT == CONVROT_LAYOUT_NK) {
       const uint64_t dims[2] = {static_cast<uint64_t>(p.K / 2), static_cast<uint64_t>(p.N)};
       const uint64_t strides[1] = {static_cast<uint64_t>(p.K / 2)};
-      const uint32_t box[2] = {pair::BK / 2, 128};
+      const uint32_t box[2] = {KS / 2, 128};
       rc = make_tmap_u8(&map_b, p.qweight, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     } else {
       const uint64_t dims[2] = {static_cast<uint64_t>(p.N / 2), static_cast<uint64_t>(p.K)};
       const uint64_t strides[1] = {static_cast<uint64_t>(p.N / 2)};
-      const uint32_t box[2] = {64, pair::BK};
+      const uint32_t box[2] = {64, KS};
       rc = make_tmap_u8(&map_b, p.qweight, 2, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     }
     if (rc != CONVROT_OK) return rc;
   }
-  auto kernel = pair::pair_gemm_kernel<LAYOUT, TOut>;
+  auto kernel = pair::pair_gemm_kernel<LAYOUT, TOut, KIND>;
   CONVROT_CUDA_CHECK(
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pair::kSmemBytes)));
   const int tiles = p.m_tiles * p.n_tiles;
@@ -1012,6 +1117,55 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
     case CONVROT_F16: return w4a4::launch<CONVROT_LAYOUT_KN, __half>(map, p, s);
     default: return w4a4::launch<CONVROT_LAYOUT_KN, float>(map, p, s);
   }
+}
+
+// W4A16: rotated bf16 / fp16 activations x packed int4 weights (core.py:1123-1152).
+int convrot_w4a16_gemm(const void* act, int act_dtype, const uint8_t* qweight, int layout, const float* wscales,
+                       const float* bias, void* out, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
+  using namespace convrot;
+  CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || layout == CONVROT_LAYOUT_KN, CONVROT_ERR_INVALID, "unknown layout %d",
+                  layout);
+  CONVROT_REQUIRE(act_dtype == CONVROT_BF16 || act_dtype == CONVROT_F16, CONVROT_ERR_INVALID,
+                  "W4A16 activations must be bfloat16 or float16 (dtype %d)", act_dtype);
+  CONVROT_REQUIRE(valid_dtype(out_dtype), CONVROT_ERR_INVALID, "unknown output dtype %d", out_dtype);
+  CONVROT_REQUIRE(m >= 0 && n > 0 && k > 0, CONVROT_ERR_INVALID, "invalid shape m=%lld n=%lld k=%lld",
+                  static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  CONVROT_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CONVROT_ERR_UNSUPPORTED, "shape too large");
+  CONVROT_REQUIRE(k % 64 == 0, CONVROT_ERR_UNSUPPORTED,
+                  "the W4A16 kernel needs K divisible by 64 (TMA chunks of 64 16-bit values), got %lld",
+                  static_cast<long long>(k));
+  CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || n % 32 == 0, CONVROT_ERR_UNSUPPORTED,
+                  "the W4A16 kernel needs N divisible by 32 for K x packed-N weights (16-byte rows), got %lld",
+                  static_cast<long long>(n));
+  if (m == 0) return CONVROT_OK;
+  CONVROT_REQUIRE(act && qweight && wscales && out, CONVROT_ERR_INVALID, "null pointer");
+  CONVROT_REQUIRE(aligned_to(act, 16) && aligned_to(qweight, 16) && aligned_to(out, 16), CONVROT_ERR_INVALID,
+                  "activation, weight and output must be 16-byte aligned");
+  w4a4::Params p;
+  p.qweight = qweight;
+  p.xscales = nullptr;
+  p.wscales = wscales;
+  p.bias = bias;
+  p.out = out;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.layout = layout;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using namespace w4a4;
+#define CONVROT_W4A16_OUT(L, KIND)                                                    \
+  switch (out_dtype) {                                                                \
+    case CONVROT_BF16: return launch_pair<L, __nv_bfloat16, pair::KIND>(act, p, s);   \
+    case CONVROT_F16: return launch_pair<L, __half, pair::KIND>(act, p, s);           \
+    default: return launch_pair<L, float, pair::KIND>(act, p, s);                     \
+  }
+  if (layout == CONVROT_LAYOUT_NK) {
+    if (act_dtype == CONVROT_BF16) { CONVROT_W4A16_OUT(CONVROT_LAYOUT_NK, KIND_BF16) }
+    CONVROT_W4A16_OUT(CONVROT_LAYOUT_NK, KIND_F16)
+  }
+  if (act_dtype == CONVROT_BF16) { CONVROT_W4A16_OUT(CONVROT_LAYOUT_KN, KIND_BF16) }
+  CONVROT_W4A16_OUT(CONVROT_LAYOUT_KN, KIND_F16)
+#undef CONVROT_W4A16_OUT
 }
 
 // Read and clear the device-side error word set by a kernel whose bounded

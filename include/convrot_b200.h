@@ -123,6 +123,22 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout,
                       void* stream);
 
 /*
+ * W4A16 linear: out[m, n] = T(fl(dots[m, n] * wscales[n]) + bias[n]) with
+ * dots = sum_k act[m, k] * w[k, n] accumulated in float32 (tcgen05
+ * kind::f16; the nibbles are expanded to exact 16-bit integers in shared
+ * memory).  Replaces mpp_w4a16_matmul (core.py:1123-1152; Metal K7
+ * core.py:877-912, launched at core.py:961-969).  act: (m, k) rotated activations of act_dtype (bfloat16
+ * or float16); qweight: packed `layout` (the reference passes K x packed-N);
+ * wscales / bias (n,) float32 (bias may be NULL); out: (m, n) of out_dtype.
+ * k % 64 == 0; layout KN needs n % 32 == 0 (16-byte weight rows for TMA).
+ * The summation order differs from the reference's float32 matmul: results
+ * agree to float32 rounding, not bit for bit.
+ */
+int convrot_w4a16_gemm(const void* act, int act_dtype, const uint8_t* qweight, int layout,
+                       const float* wscales, const float* bias, void* out, int out_dtype,
+                       int64_t m, int64_t n, int64_t k, void* stream);
+
+/*
  * Diagnostics: every wait inside the tcgen05 kernels is bounded; a kernel
  * whose wait times out stops early and records a non-zero code in a
  * device-side word.  This reads and clears that word (0 = no time-out).  It

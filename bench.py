@@ -355,6 +355,28 @@ def run_ours(args, rank, world, local):
     dense_tflops = ops / (dense_ms * 1e-3) / 1e12
     del dgraph
 
+    # ---- W4A16 backend (rotate, then the kind::f16 GEMM) on the same sweep and weights
+    rot_bufs = [torch.empty((m, k), dtype=torch.bfloat16, device=device) for (m, k, n) in shapes]
+    out16 = [torch.empty((m, n), dtype=torch.bfloat16, device=device) for (m, k, n) in shapes]
+
+    def w4a16_step():
+        s = _lib.stream_of(xs_dev[0])
+        for j, ((m, k, n), x) in enumerate(zip(shapes, xs_dev)):
+            layer = layers[(k, n)]
+            _lib.check(lib.convrot_rotate(_lib.ptr(x), _lib.BF16, m, k, GROUP, _lib.ptr(rot_bufs[j]), s), "rotate")
+            _lib.check(lib.convrot_w4a16_gemm(_lib.ptr(rot_bufs[j]), _lib.BF16, _lib.ptr(layer.qweight), _lib.LAYOUT_KN,
+                                              _lib.ptr(layer.scales), _lib.ptr(layer.bias), _lib.ptr(out16[j]),
+                                              _lib.BF16, m, n, k, s), "w4a16 gemm")
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            w4a16_step()
+    torch.cuda.synchronize()
+    g16 = capture(w4a16_step)
+    replay_ms(g16, 1)
+    w4a16_ms = replay_ms(g16, args.steps) / args.steps
+    del g16, rot_bufs, out16
+
     # ---- end to end through the public API with host buffers
     e2e = run_e2e(args, shapes, layers, xs_dev, device, world)
 
@@ -400,6 +422,9 @@ def run_ours(args, rank, world, local):
         "dense_bf16": {"value": round(dense_tflops, 1), "unit": "TFLOP/s", "ms_per_step": round(dense_ms, 4),
                        "impl": "torch.addmm bf16 (cuBLAS), same sweep, graph-captured"},
         "speedup_vs_dense_bf16": round(dense_ms / ms_per_step, 3),
+        "w4a16": {"value": round(ops / (w4a16_ms * 1e-3) / 1e12, 1), "unit": UNIT, "ms_per_step": round(w4a16_ms, 4),
+                  "speedup_vs_dense_bf16": round(dense_ms / w4a16_ms, 3),
+                  "impl": "rotate (prep kernel) + W4A16 tcgen05 kind::f16 GEMM, same sweep and weights, graph-captured"},
         "roofline": roofline, "roofline_prep": roofline_prep,
         "e2e": e2e,
         "gpu_launches": 2 * len(shapes) * args.steps,

@@ -47,7 +47,7 @@ def _sha(a: np.ndarray) -> str:
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="checkout of Lumenbeing/convrot-mlx")
     parser.add_argument("--out", default=str(HERE))
     args = parser.parse_args()
 

@@ -76,6 +76,8 @@ struct alignas(8) Barriers {
 constexpr int kEpiBytes = kEpiWarps * 2 * BN * 4;  // ws and bias, one copy per epilogue warp
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBBytes) + kEpiBytes + sizeof(Barriers);
 
+constexpr int kMaxOuts = 8;
+
 struct Params {
   const uint8_t* qweight;
   const float* xscales;
@@ -85,6 +87,14 @@ struct Params {
   int M, N, K;
   int m_tiles, n_tiles, k_blocks;
   int layout;
+  // Extra destinations of the pair kernel's epilogue (tensor-parallel
+  // all-gather): with n_outs > 0, element (m, n) goes to outs[i][m * ldc +
+  // col_off + n] for every i (this GPU's buffer and peers' buffers mapped
+  // into this GPU's address space), and `out` is unused.
+  void* outs[kMaxOuts] = {};
+  int n_outs = 0;
+  int64_t ldc = 0;
+  int64_t col_off = 0;
 };
 
 // Wait for the phase of `bar` with parity `parity` to complete, for at most
@@ -863,8 +873,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
       const bool row_ok = m < p.M;
       const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
-      TOut* orow = static_cast<TOut*>(p.out) + static_cast<int64_t>(row_ok ? m : 0) * p.N;
-      const bool vec_store = (p.N % (16 / sizeof(TOut))) == 0;
+      const bool gather = p.n_outs > 0;
+      const int64_t ldc = gather ? p.ldc : p.N;
+      const int64_t row_off = static_cast<int64_t>(row_ok ? m : 0) * ldc + (gather ? p.col_off : 0);
+      TOut* orow = static_cast<TOut*>(p.out) + row_off;
+      const bool vec_store = ((gather ? (ldc | p.col_off) : p.N) % (16 / sizeof(TOut))) == 0;
       const uint32_t t_row = tmem_base + ((ew * 32u) << 16) + buf * BN;
       for (int c = 0; c < BN / 32; ++c) {
         const int n = n_blk * BN + c * 32;
@@ -893,7 +906,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!row_ok) continue;
-        if (vec_store && n + 32 <= p.N) {
+        if (gather) {
+          // this tile's columns into every destination (peers over NVLink)
+#pragma unroll 1
+          for (int d = 0; d < p.n_outs; ++d) {
+            TOut* drow = static_cast<TOut*>(p.outs[d]) + row_off;
+            if (vec_store && n + 32 <= p.N) {
+              store16(drow + n, v, 0);
+              store16(drow + n + 16, v, 16);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) drow[n + j] = cvt_out<TOut>(v[j]);
+            }
+          }
+        } else if (vec_store && n + 32 <= p.N) {
           store16(orow + n, v, 0);
           store16(orow + n + 16, v, 16);
         } else {
@@ -906,6 +933,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(lead_empty0 + buf * 8);
     }
+    // peers read the gathered output after a flag barrier that follows this
+    // kernel: make this thread's stores to their memory visible system-wide
+    if (p.n_outs > 0) __threadfence_system();
   }
 
   __syncwarp();
@@ -1116,6 +1146,62 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
     case CONVROT_BF16: return w4a4::launch<CONVROT_LAYOUT_KN, __nv_bfloat16>(map, p, s);
     case CONVROT_F16: return w4a4::launch<CONVROT_LAYOUT_KN, __half>(map, p, s);
     default: return w4a4::launch<CONVROT_LAYOUT_KN, float>(map, p, s);
+  }
+}
+
+// Tensor-parallel W4A4: this rank's column shard, all-gathered by the epilogue.
+int convrot_w4a4_gemm_gather(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
+                             const float* wscales, const float* bias, void* const* outs, int n_outs, int64_t ldc,
+                             int64_t col_offset, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
+  using namespace convrot;
+  CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || layout == CONVROT_LAYOUT_KN, CONVROT_ERR_INVALID, "unknown layout %d",
+                  layout);
+  CONVROT_REQUIRE(valid_dtype(out_dtype), CONVROT_ERR_INVALID, "unknown output dtype %d", out_dtype);
+  CONVROT_REQUIRE(m >= 0 && n > 0 && k > 0, CONVROT_ERR_INVALID, "invalid shape m=%lld n=%lld k=%lld",
+                  static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  CONVROT_REQUIRE(outs != nullptr && n_outs >= 1 && n_outs <= w4a4::kMaxOuts, CONVROT_ERR_INVALID,
+                  "n_outs must be in [1, %d], got %d", w4a4::kMaxOuts, n_outs);
+  CONVROT_REQUIRE(col_offset >= 0 && ldc >= col_offset + n, CONVROT_ERR_INVALID,
+                  "ldc %lld too small for column offset %lld + n %lld", static_cast<long long>(ldc),
+                  static_cast<long long>(col_offset), static_cast<long long>(n));
+  CONVROT_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CONVROT_ERR_UNSUPPORTED, "shape too large");
+  CONVROT_REQUIRE(w4a4::pair_supported(layout, n, k), CONVROT_ERR_UNSUPPORTED,
+                  "the gathering GEMM needs K %% 128 == 0 and, for K x packed-N, N %% 32 == 0 (m=%lld n=%lld k=%lld)",
+                  static_cast<long long>(m), static_cast<long long>(n), static_cast<long long>(k));
+  if (m == 0) return CONVROT_OK;
+  CONVROT_REQUIRE(act && qweight && xscales && wscales, CONVROT_ERR_INVALID, "null pointer");
+  CONVROT_REQUIRE(aligned_to(act, 16) && aligned_to(qweight, 16), CONVROT_ERR_INVALID,
+                  "activation and weight must be 16-byte aligned");
+  w4a4::Params p;
+  p.qweight = qweight;
+  p.xscales = xscales;
+  p.wscales = wscales;
+  p.bias = bias;
+  p.M = static_cast<int>(m);
+  p.N = static_cast<int>(n);
+  p.K = static_cast<int>(k);
+  p.layout = layout;
+  for (int d = 0; d < n_outs; ++d) {
+    CONVROT_REQUIRE(outs[d] != nullptr, CONVROT_ERR_INVALID, "null destination %d", d);
+    p.outs[d] = outs[d];
+  }
+  p.out = outs[0];
+  p.n_outs = n_outs;
+  p.ldc = ldc;
+  p.col_off = col_offset;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  using namespace w4a4;
+  if (layout == CONVROT_LAYOUT_NK) {
+    switch (out_dtype) {
+      case CONVROT_BF16: return launch_pair<CONVROT_LAYOUT_NK, __nv_bfloat16>(act, p, s);
+      case CONVROT_F16: return launch_pair<CONVROT_LAYOUT_NK, __half>(act, p, s);
+      default: return launch_pair<CONVROT_LAYOUT_NK, float>(act, p, s);
+    }
+  }
+  switch (out_dtype) {
+    case CONVROT_BF16: return launch_pair<CONVROT_LAYOUT_KN, __nv_bfloat16>(act, p, s);
+    case CONVROT_F16: return launch_pair<CONVROT_LAYOUT_KN, __half>(act, p, s);
+    default: return launch_pair<CONVROT_LAYOUT_KN, float>(act, p, s);
   }
 }
 

@@ -1,0 +1,173 @@
+"""Tensor-parallel ConvRot W4A4 linear: column split of N over the GPUs of one node.
+
+The multi-GPU form of ``ConvRotLinear`` (core.py:1213-1313 of the reference,
+which runs on a single Apple GPU).  Rank r of a process group of ``world``
+GPUs owns output columns ``[r * N / world, (r + 1) * N / world)``: that slice
+of the packed weight (K x packed-N: a column slice of the bytes; N x
+packed-K: a row slice), of the weight scales and of the bias.  The
+activation is replicated and every rank runs the fused rotate + quantize on
+it (cheaper than broadcasting the codes).  The rank's GEMM
+(``convrot_w4a4_gemm_gather``) stores each output tile into every rank's full
+(M, N) output buffer -- its own and, through symmetric memory, its peers' --
+so the all-gather over NVLink overlaps the GEMM; a flag barrier
+(``convrot_peer_barrier``) then makes every rank's full output visible.
+
+Buffers are symmetric-memory tensors (``torch.distributed._symmetric_memory``,
+CUDA backend, multicast off) allocated once per (rows, dtype).  Outputs
+alternate between two buffers: a rank that has passed call i + 1's barrier
+knows every rank has finished call i (whose output it may still be reading
+until its own call i + 1), so call i + 2 may overwrite buffer i % 2.  The
+tensor returned by ``forward`` is therefore valid until the call after next.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import _lib
+from .core import (
+    CONVROT_GROUP_SIZE,
+    ConvRotLinear,
+    _dtype_code,
+    _f32_vec,
+    _prepare,
+)
+
+_MAX_WORLD = 8
+
+
+def shard_range(out_features: int, world: int, rank: int, layout: int) -> tuple[int, int]:
+    """Columns ``[start, stop)`` owned by ``rank``.
+
+    N must split evenly; for K x packed-N weights each shard must also be a
+    whole number of 16-byte rows (N / world % 32 == 0), as the two-CTA GEMM
+    reads weight rows with TMA.
+    """
+
+    if not 1 <= world <= _MAX_WORLD:
+        raise ValueError(f"world size must be in [1, {_MAX_WORLD}], got {world}")
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside [0, {world})")
+    if out_features % world:
+        raise ValueError(f"out_features {out_features} does not split over {world} ranks")
+    shard = out_features // world
+    if layout == _lib.LAYOUT_KN and shard % 32:
+        raise ValueError(f"K x packed-N shards need out_features / world % 32 == 0, got {shard}")
+    return rank * shard, (rank + 1) * shard
+
+
+def shard_weight(qweight: torch.Tensor, layout: int, start: int, stop: int) -> torch.Tensor:
+    """The packed weight of columns [start, stop) (both even)."""
+
+    if start % 2 or stop % 2:
+        raise ValueError("shard bounds must be even (two columns per packed byte)")
+    if layout == _lib.LAYOUT_KN:
+        return qweight[:, start // 2 : stop // 2].contiguous()
+    return qweight[start:stop].contiguous()
+
+
+class ColumnParallelConvRotLinear(nn.Module):
+    """One rank's shard of a ConvRotLinear split over N (see the module doc)."""
+
+    def __init__(self, in_features: int, out_features: int, *, group: dist.ProcessGroup | None = None,
+                 bias: bool = True, group_size: int = CONVROT_GROUP_SIZE, backend: str = "mpp-w4a4",
+                 device=None) -> None:
+        super().__init__()
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        self.in_features = in_features
+        self.out_features = out_features
+        self.group_size = group_size
+        if backend == "mpp-w4a16":
+            raise ValueError("the tensor-parallel layer implements the W4A4 backends")
+        local = ConvRotLinear(in_features, out_features, bias=bias, group_size=group_size, backend=backend,
+                              device=device)
+        self.layout = local.layout_code
+        self.start, self.stop = shard_range(out_features, self.world, self.rank, self.layout)
+        self.shard_features = self.stop - self.start
+        self.register_buffer("qweight", shard_weight(local.qweight, self.layout, self.start, self.stop))
+        self.register_buffer("scales", local.scales[self.start : self.stop].clone())
+        self.register_buffer("bias", local.bias[self.start : self.stop].clone())
+        self.source_has_bias = bias
+        self._out = {}      # (rows, dtype) -> two (tensor, peer pointer array, handle)
+        self._flags = None  # (tensor, peer pointer array)
+        self._epoch = 0     # barrier epoch (never 0)
+        self._calls = 0     # output buffer = calls % 2
+
+    @classmethod
+    def from_full(cls, layer: ConvRotLinear, group: dist.ProcessGroup | None = None) -> "ColumnParallelConvRotLinear":
+        """Shard a full (already quantized) ConvRotLinear on every rank."""
+
+        tp = cls(layer.in_features, layer.out_features, group=group, bias=layer.source_has_bias,
+                 group_size=layer.group_size, backend=layer.backend, device=layer.qweight.device)
+        tp.qweight = shard_weight(layer.qweight, tp.layout, tp.start, tp.stop)
+        tp.scales = _f32_vec(layer.scales)[tp.start : tp.stop].clone()
+        tp.bias = _f32_vec(layer.bias)[tp.start : tp.stop].clone()
+        return tp
+
+    # -- symmetric buffers ---------------------------------------------------
+
+    def _symmetric(self, shape, dtype):
+        import torch.distributed._symmetric_memory as symm
+
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")  # plain peer stores only
+        try:
+            symm.set_backend("CUDA")
+        except Exception:  # already set
+            pass
+        t = symm.empty(*shape, dtype=dtype, device=self.qweight.device)
+        handle = symm.rendezvous(t, self.group)
+        ptrs = (ctypes.c_void_p * self.world)(*[int(p) for p in handle.buffer_ptrs])
+        return t, ptrs, handle
+
+    def _output(self, rows: int, dtype: torch.dtype, which: int):
+        key = (rows, dtype)
+        if key not in self._out:
+            self._out[key] = [self._symmetric((rows, self.out_features), dtype) for _ in range(2)]
+        return self._out[key][which]
+
+    def _flag_arrays(self):
+        if self._flags is None:
+            t, ptrs, handle = self._symmetric((self.world,), torch.int32)
+            t.zero_()
+            torch.cuda.synchronize(t.device)
+            dist.barrier(self.group)  # every rank's flags are zero before any barrier kernel runs
+            self._flags = (t, ptrs, handle)
+        return self._flags
+
+    # -- forward ---------------------------------------------------------------
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"ConvRotLinear expected K={self.in_features}, got {x.shape[-1]}")
+        lead = x.shape[:-1]
+        x2d = x.reshape(-1, self.in_features)
+        m = x2d.shape[0]
+        _, flag_ptrs, _ = self._flag_arrays()
+        self._epoch = (self._epoch % 0x7FFFFFFF) + 1
+        self._calls += 1
+        out, out_ptrs, _ = self._output(m, x.dtype, self._calls & 1)
+        lib = _lib.load()
+        stream = _lib.stream_of(x2d)
+        codes, xscales = _prepare(x2d, self.group_size, packed=False)
+        _lib.check(
+            lib.convrot_w4a4_gemm_gather(
+                _lib.ptr(codes), _lib.ptr(self.qweight), self.layout, _lib.ptr(xscales), _lib.ptr(self.scales),
+                _lib.ptr(self.bias), out_ptrs, self.world, self.out_features, self.start, _dtype_code(x.dtype),
+                m, self.shard_features, self.in_features, stream,
+            ),
+            "tensor-parallel W4A4 GEMM",
+        )
+        _lib.check(lib.convrot_peer_barrier(ctypes.cast(flag_ptrs, ctypes.POINTER(ctypes.c_void_p)), self.world,
+                                            self.rank, self._epoch, stream), "peer barrier")
+        return out.reshape(*lead, self.out_features)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, world={self.world}, "
+                f"rank={self.rank}, columns=[{self.start}, {self.stop})")

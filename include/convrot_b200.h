@@ -139,6 +139,37 @@ int convrot_w4a16_gemm(const void* act, int act_dtype, const uint8_t* qweight, i
                        int64_t m, int64_t n, int64_t k, void* stream);
 
 /*
+ * Tensor-parallel W4A4 (column split of N across the GPUs of one node): the
+ * GEMM of this rank's shard -- qweight / wscales / bias hold columns
+ * [col_offset, col_offset + n) of the full layer -- whose epilogue writes
+ * every output tile into each of the n_outs (1..8) destinations at
+ * dst[i * ldc + col_offset + j]: this GPU's full (m, ldc) output and the
+ * peers' (device pointers valid on this GPU, e.g. symmetric memory), so the
+ * all-gather of the outputs over NVLink overlaps the GEMM tile by tile.
+ * Follow it with convrot_peer_barrier before any rank reads its full output.
+ * No reference counterpart: the reference runs on one Apple GPU; this is the
+ * multi-GPU form of mpp_w4a4_int8_matmul (core.py:1088-1120).  Needs
+ * k % 128 == 0 and, for KN, n % 32 == 0.  outs: host array of n_outs device
+ * pointers.
+ */
+int convrot_w4a4_gemm_gather(const int8_t* act, const uint8_t* qweight, int layout,
+                             const float* xscales, const float* wscales, const float* bias,
+                             void* const* outs, int n_outs, int64_t ldc, int64_t col_offset,
+                             int out_dtype, int64_t m, int64_t n, int64_t k, void* stream);
+
+/*
+ * Flag barrier across `world` (1..8) GPUs of one node.  flag_arrays: host
+ * array of `world` device pointers, valid on this GPU, to each rank's
+ * (world,) uint32 flag array (zero-initialised, mapped by every rank).
+ * Writes `epoch` (> 0, increasing per call) into slot `rank` of every array
+ * with system-scope release stores, then waits, bounded by 2 s, until this
+ * rank's array holds `epoch` in every slot (device error code 31 on time-out,
+ * see convrot_take_device_error).  No reference counterpart.
+ */
+int convrot_peer_barrier(uint32_t* const* flag_arrays, int world, int rank, uint32_t epoch,
+                         void* stream);
+
+/*
  * Diagnostics: every wait inside the tcgen05 kernels is bounded; a kernel
  * whose wait times out stops early and records a non-zero code in a
  * device-side word.  This reads and clears that word (0 = no time-out).  It

@@ -564,6 +564,101 @@ def run_reference(args, rank, world):
     }
 
 
+VIDEO_M = 32760
+VIDEO_KN = ((5120, 15360), (5120, 13824), (13824, 5120))
+
+
+def run_video_tp(args, rank, world, local):
+    """large video-DiT linears, weights N-split over the
+    ranks (ColumnParallelConvRotLinear), the all-gather of the outputs fused
+    into the GEMM epilogue (peer stores) plus a flag barrier.  One step = the
+    three linears on M = 32760 tokens.  Timed eagerly (the barrier epoch
+    advances every call) with CUDA events, max over ranks; also timed with
+    each rank's GEMMs writing only its own shard (no exchange) for the split."""
+
+    import ctypes
+
+    import convrot_mlx_b200 as cr
+    from convrot_mlx_b200 import _lib
+    from convrot_mlx_b200.tp import ColumnParallelConvRotLinear
+
+    device = torch.device("cuda", local if world > 1 else 0)
+    if world == 1 and not torch.distributed.is_initialized():
+        # the layer keeps its output in symmetric memory, which needs a process group
+        import datetime
+        import socket
+
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        torch.distributed.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                             timeout=datetime.timedelta(seconds=120), device_id=device)
+    layers, xs = [], []
+    for i, (k, n) in enumerate(VIDEO_KN):
+        full, _, _ = make_linear(k, n, SEED + 50 + i, device)
+        layers.append(ColumnParallelConvRotLinear.from_full(full))
+        del full
+        xs.append(make_activation(VIDEO_M, k, SEED + 60 + i, device))
+    torch.cuda.synchronize()
+    lib = _lib.load()
+
+    def step():
+        for layer, x in zip(layers, xs):
+            layer(x)
+
+    def local_only():
+        # the same GEMMs writing only this rank's shard into its own buffer
+        for layer, x in zip(layers, xs):
+            out, _, _ = layer._output(VIDEO_M, x.dtype, 0)
+            codes, xsc = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
+            one = (ctypes.c_void_p * 1)(out.data_ptr())
+            _lib.check(lib.convrot_w4a4_gemm_gather(_lib.ptr(codes), _lib.ptr(layer.qweight), layer.layout,
+                                                    _lib.ptr(xsc), _lib.ptr(layer.scales), _lib.ptr(layer.bias), one, 1,
+                                                    layer.out_features, layer.start, _lib.BF16, VIDEO_M,
+                                                    layer.shard_features, layer.in_features, _lib.stream_of(x)), "gemm")
+
+    def timed(fn, steps):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+        return max_over_ranks(e0.elapsed_time(e1), world)
+
+    with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
+        elapsed_ms = timed(step, args.steps)
+    local_ms = timed(local_only, args.steps) / args.steps
+    ops = sum(2 * VIDEO_M * k * n for k, n in VIDEO_KN)
+    ms_per_step = elapsed_ms / args.steps
+    err = _lib.take_device_error()
+    line = {
+        "metric": "video-DiT linears W4A4 tensor-parallel TOPS (BASELINE config 5)",
+        "value": round(ops / (ms_per_step * 1e-3) / 1e12, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8 (A4 codes x W4 nibbles, int32 accumulate), bf16 I/O",
+        "data": "synthetic, seeded: W ~ N(0, 0.02), bias ~ N(0, 0.01), x ~ N(0, 1) with 1% outlier channels x20",
+        "config": {"workload": "video-tp (BASELINE config 5)", "m": VIDEO_M, "kn": [list(p) for p in VIDEO_KN],
+                   "group_size": GROUP, "parallelism": f"tp{world} (N split, all-gather fused into the GEMM epilogue)",
+                   "timing": "eager launches between CUDA events, max over ranks"},
+        "compute_only_ms_per_step": round(local_ms, 4),
+        "exchange_overhead_ms_per_step": round(ms_per_step - local_ms, 4),
+        "gathered_bytes_per_rank_per_step": sum(VIDEO_M * n * 2 * (world - 1) // world for k, n in VIDEO_KN),
+        "gpu_launches": 3 * 3 * args.steps,
+        "clocks": dict(clocks.summary(), window="nvidia-smi samples during the timed steps"),
+        "device_error": err,
+    }
+    for layer in layers:
+        layer._out.clear()
+        layer._flags = None
+    return line
+
+
 def run_case(args):
     """One kernel on one shape, launched ``--case-launches`` times on the
     default stream (eager), for profilers: ``--case gemm`` runs the W4A4 GEMM
@@ -600,6 +695,8 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--workload", choices=("flux-sweep", "video-tp"), default="flux-sweep",
+                    help="flux-sweep: BASELINE config 3 (default); video-tp: config 5, tensor-parallel over --gpus")
     ap.add_argument("--case", choices=("gemm", "prep"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=3072)
@@ -620,11 +717,12 @@ def main(argv=None):
         return 0
     rank, world, local = dist_setup(args.gpus)
     try:
-        line = run_ours(args, rank, world, local)
+        line = run_video_tp(args, rank, world, local) if args.workload == "video-tp" else run_ours(args, rank, world,
+                                                                                                   local)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
-        if world > 1:
+        if torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()
     return 0
 

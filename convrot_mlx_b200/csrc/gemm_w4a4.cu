@@ -501,6 +501,7 @@ constexpr int kB8Bytes = 128 * BK;        // 32 KB
 constexpr int kItems = kBpBytes / 16;     // 1024 transform items per stage
 constexpr int kItemsPerThread = kItems / kXThreads;  // 8
 constexpr int kEpiBytes = kEWarps * 2 * BN * 4;
+constexpr int kStageOutBytes = kEWarps * 32 * 64;  // per epilogue warp: 32 rows x 32 16-bit columns
 constexpr uint32_t kTmemCols = 2 * BN;
 
 // Operand kinds.  KIND_I8: A4 int8 codes x nibbles expanded to int8 x 16
@@ -530,7 +531,9 @@ struct alignas(16) Bars {
   int err;
 };
 
-constexpr size_t kSmemBytes = 1024 + S * (kABytes + kBpBytes) + B8 * kB8Bytes + kEpiBytes + sizeof(Bars);
+constexpr size_t kSmemBytes =
+    1024 + S * (kABytes + kBpBytes) + B8 * kB8Bytes + kEpiBytes + kStageOutBytes + sizeof(Bars);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 // Waits use cluster-scope acquire: most barriers of the pair kernel receive
 // arrivals from the other CTA.
@@ -594,7 +597,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB8 = sA + S * kABytes;                      // B8 x 32 KB
   uint8_t* sBp = sB8 + B8 * kB8Bytes;                   // S x 16 KB
   float* epi = reinterpret_cast<float*>(sBp + S * kBpBytes);
-  Bars* bars = reinterpret_cast<Bars*>(reinterpret_cast<uint8_t*>(epi) + kEpiBytes);
+  uint8_t* stage_out = reinterpret_cast<uint8_t*>(epi) + kEpiBytes;  // gather path: row-major restaging
+  Bars* bars = reinterpret_cast<Bars*>(stage_out + kStageOutBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -903,6 +907,44 @@ __global__ void __launch_bounds__(kThreads, 1)
               // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
               v[j + u] = __fadd_rn(__fmul_rn(__uint_as_float(r[j + u]), wv[u]), bv[u]);
             }
+          }
+        }
+        if constexpr (sizeof(TOut) == 2) {
+          if (gather && vec_store && n + 32 <= p.N) {  // warp-uniform; every lane takes part
+            // Peer stores: lane = row gives 32 scattered 16-byte pieces per
+            // instruction, which NVLink carries badly.  Restage the warp's
+            // 32 x 32 chunk in shared memory (16-byte chunk q of row r at
+            // ((q + r / 2) % 4) -- conflict-free both ways) and store it with
+            // four lanes per row: 64 contiguous bytes per row, 8 rows per
+            // instruction.
+            const uint32_t sb = smem_u32(stage_out) + ew * 2048;
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              sts128(sb + lane * 64 + (((q + (lane >> 1)) & 3) << 4), pack2<TOut>(v[8 * q], v[8 * q + 1]),
+                     pack2<TOut>(v[8 * q + 2], v[8 * q + 3]), pack2<TOut>(v[8 * q + 4], v[8 * q + 5]),
+                     pack2<TOut>(v[8 * q + 6], v[8 * q + 7]));
+            __syncwarp();
+            uint4 piece[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = i * 8 + (lane >> 2), q = lane & 3;
+              const uint32_t a = sb + r * 64 + (((q + (r >> 1)) & 3) << 4);
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(piece[i].x), "=r"(piece[i].y), "=r"(piece[i].z), "=r"(piece[i].w)
+                           : "r"(a));
+            }
+            const int64_t row0 = static_cast<int64_t>(m_blk * BM + 128 * rank + ew * 32);
+#pragma unroll 1
+            for (int d = 0; d < p.n_outs; ++d) {
+              TOut* base = static_cast<TOut*>(p.outs[d]) + p.col_off + n + (lane & 3) * 8;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int64_t r = row0 + i * 8 + (lane >> 2);
+                if (r < p.M) *reinterpret_cast<uint4*>(base + r * ldc) = piece[i];
+              }
+            }
+            continue;
           }
         }
         if (!row_ok) continue;

@@ -910,9 +910,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if constexpr (sizeof(TOut) == 2) {
-          if (gather && vec_store && n + 32 <= p.N) {  // warp-uniform; every lane takes part
-            // Peer stores: lane = row gives 32 scattered 16-byte pieces per
-            // instruction, which NVLink carries badly.  Restage the warp's
+          if (vec_store && n + 32 <= p.N) {  // warp-uniform; every lane takes part
+            // lane = row would give 32 scattered 16-byte pieces per store
+            // instruction (NVLink carries those badly, L2 merges them at a
+            // cost).  Restage the warp's
             // 32 x 32 chunk in shared memory (16-byte chunk q of row r at
             // ((q + r / 2) % 4) -- conflict-free both ways) and store it with
             // four lanes per row: 64 contiguous bytes per row, 8 rows per
@@ -935,9 +936,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                            : "r"(a));
             }
             const int64_t row0 = static_cast<int64_t>(m_blk * BM + 128 * rank + ew * 32);
+            const int n_dst = gather ? p.n_outs : 1;
 #pragma unroll 1
-            for (int d = 0; d < p.n_outs; ++d) {
-              TOut* base = static_cast<TOut*>(p.outs[d]) + p.col_off + n + (lane & 3) * 8;
+            for (int d = 0; d < n_dst; ++d) {
+              TOut* base = static_cast<TOut*>(gather ? p.outs[d] : p.out) + (gather ? p.col_off : 0) + n +
+                           (lane & 3) * 8;
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const int64_t r = row0 + i * 8 + (lane >> 2);

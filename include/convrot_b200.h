@@ -170,6 +170,33 @@ int convrot_peer_barrier(uint32_t* const* flag_arrays, int world, int rank, uint
                          void* stream);
 
 /*
+ * The W4A4 linear in one call that allocates nothing: convrot_prepare_i8
+ * followed by convrot_w4a4_gemm, with the int8 codes and row scales between
+ * them kept in a fixed device array inside the library instead of a buffer
+ * from the caller.  It is for callers that cannot allocate device memory: a
+ * plugin that its host engine hands only input and output buffers, or code
+ * whose host framework reserves the device's memory for its own allocator.
+ * No counterpart in the reference (there the framework allocates).
+ *   - The array holds CONVROT_LINEAR_STATIC_SCRATCH_BYTES: the codes of
+ *     m x k (rounded up to 256 bytes) plus 4 * m bytes of scales must fit
+ *     (m x k up to about 67 million), else CONVROT_ERR_UNSUPPORTED.  Every
+ *     GPU that loads the library holds the array until the process exits.
+ *   - The first call on a device looks up the array's device address on
+ *     that device (make it before any stream capture on the device).
+ *   - All calls share the one array: calls whose work overlaps on the GPU
+ *     (different streams, or other host threads) race and must not overlap.
+ *     Every call rewrites all of the array it reads, so nothing from an
+ *     earlier call carries over.
+ * Arguments as convrot_prepare_i8 (x, x_dtype, group_size) and
+ * convrot_w4a4_gemm (qweight ... stream).
+ */
+#define CONVROT_LINEAR_STATIC_SCRATCH_BYTES (64LL << 20)
+int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
+                               const uint8_t* qweight, int layout, const float* wscales,
+                               const float* bias, void* out, int out_dtype, int64_t m, int64_t n,
+                               int64_t k, void* stream);
+
+/*
  * Diagnostics: every wait inside the tcgen05 kernels is bounded; a kernel
  * whose wait times out stops early and records a non-zero code in a
  * device-side word.  This reads and clears that word (0 = no time-out).  It

@@ -564,6 +564,317 @@ def run_reference(args, rank, world):
     }
 
 
+# ---------------------------------------------------------------------------
+# a random-init FLUX.1-dev-architecture DiT (the
+# reference runs FLUX through Apple's MLX example, examples/flux1_dev; the
+# model code below is written from the published architecture: 19 double-
+# stream and 38 single-stream blocks, hidden 3072, 24 heads of 128, MLP
+# ratio 4, 3-axis RoPE (16, 56, 56), 64 latent channels, 4096-wide text
+# context, 768-wide pooled vector, guidance embedding).
+
+FLUX_DEV = dict(hidden=3072, heads=24, mlp_ratio=4.0, depth=19, depth_single=38, in_channels=64, context=4096,
+                vec=768, axes=(16, 56, 56), theta=10000)
+
+
+def _rope(pos, dim, theta):
+    scale = torch.arange(0, dim, 2, dtype=torch.float64, device=pos.device) / dim
+    omega = 1.0 / (theta ** scale)
+    out = pos.to(torch.float64)[..., None] * omega
+    out = torch.stack([torch.cos(out), -torch.sin(out), torch.sin(out), torch.cos(out)], dim=-1)
+    return out.reshape(*out.shape[:-1], 2, 2).float()
+
+
+def _apply_rope(xq, xk, freqs):
+    xq_ = xq.float().reshape(*xq.shape[:-1], -1, 1, 2)
+    xk_ = xk.float().reshape(*xk.shape[:-1], -1, 1, 2)
+    xq_out = freqs[..., 0] * xq_[..., 0] + freqs[..., 1] * xq_[..., 1]
+    xk_out = freqs[..., 0] * xk_[..., 0] + freqs[..., 1] * xk_[..., 1]
+    return xq_out.reshape(*xq.shape).type_as(xq), xk_out.reshape(*xk.shape).type_as(xk)
+
+
+def _attention(q, k, v, pe):
+    q, k = _apply_rope(q, k, pe)
+    x = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+    b, h, l, d = x.shape
+    return x.transpose(1, 2).reshape(b, l, h * d)
+
+
+def _timestep_embedding(t, dim=256, max_period=10000, time_factor=1000.0):
+    import math
+
+    t = time_factor * t
+    half = dim // 2
+    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
+    args = t[:, None].float() * freqs[None]
+    return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
+
+
+class _RMSNorm(torch.nn.Module):
+    def __init__(self, dim):
+        super().__init__()
+        self.scale = torch.nn.Parameter(torch.ones(dim))
+
+    def forward(self, x):
+        return torch.nn.functional.rms_norm(x, (x.shape[-1],), self.scale.to(x.dtype), 1e-6)
+
+
+class _QKNorm(torch.nn.Module):
+    def __init__(self, dim):
+        super().__init__()
+        self.query_norm, self.key_norm = _RMSNorm(dim), _RMSNorm(dim)
+
+    def forward(self, q, k, v):
+        return self.query_norm(q).to(v.dtype), self.key_norm(k).to(v.dtype)
+
+
+class _Modulation(torch.nn.Module):
+    def __init__(self, dim, double):
+        super().__init__()
+        self.n = 6 if double else 3
+        self.lin = torch.nn.Linear(dim, self.n * dim)
+
+    def forward(self, vec):
+        return self.lin(torch.nn.functional.silu(vec))[:, None, :].chunk(self.n, dim=-1)
+
+
+class _SelfAttention(torch.nn.Module):
+    def __init__(self, dim, heads):
+        super().__init__()
+        self.heads = heads
+        self.qkv = torch.nn.Linear(dim, 3 * dim, bias=True)
+        self.norm = _QKNorm(dim // heads)
+        self.proj = torch.nn.Linear(dim, dim)
+
+
+def _split_heads(qkv, heads):
+    b, l, _ = qkv.shape
+    q, k, v = qkv.reshape(b, l, 3, heads, -1).permute(2, 0, 3, 1, 4).unbind(0)
+    return q.contiguous(), k.contiguous(), v.contiguous()
+
+
+class _DoubleBlock(torch.nn.Module):
+    def __init__(self, dim, heads, mlp):
+        super().__init__()
+        self.heads = heads
+        for side in ("img", "txt"):
+            setattr(self, f"{side}_mod", _Modulation(dim, True))
+            setattr(self, f"{side}_norm1", torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6))
+            setattr(self, f"{side}_attn", _SelfAttention(dim, heads))
+            setattr(self, f"{side}_norm2", torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6))
+            setattr(self, f"{side}_mlp", torch.nn.Sequential(torch.nn.Linear(dim, mlp), torch.nn.GELU(approximate="tanh"),
+                                                              torch.nn.Linear(mlp, dim)))
+
+    def forward(self, img, txt, vec, pe):
+        im = self.img_mod(vec)
+        tm = self.txt_mod(vec)
+        qkv = []
+        for side, x, m in (("txt", txt, tm), ("img", img, im)):
+            xm = torch.addcmul(m[0], getattr(self, f"{side}_norm1")(x), 1 + m[1])
+            attn = getattr(self, f"{side}_attn")
+            q, k, v = _split_heads(attn.qkv(xm), self.heads)
+            q, k = attn.norm(q, k, v)
+            qkv.append((q, k, v))
+        q = torch.cat([qkv[0][0], qkv[1][0]], dim=2)
+        k = torch.cat([qkv[0][1], qkv[1][1]], dim=2)
+        v = torch.cat([qkv[0][2], qkv[1][2]], dim=2)
+        a = _attention(q, k, v, pe)
+        t_len = txt.shape[1]
+        ta, ia = a[:, :t_len], a[:, t_len:]
+        img = torch.addcmul(img, im[2], self.img_attn.proj(ia))
+        img = torch.addcmul(img, im[5], self.img_mlp(torch.addcmul(im[3], self.img_norm2(img), 1 + im[4])))
+        txt = torch.addcmul(txt, tm[2], self.txt_attn.proj(ta))
+        txt = torch.addcmul(txt, tm[5], self.txt_mlp(torch.addcmul(tm[3], self.txt_norm2(txt), 1 + tm[4])))
+        return img, txt
+
+
+class _SingleBlock(torch.nn.Module):
+    def __init__(self, dim, heads, mlp):
+        super().__init__()
+        self.dim, self.heads, self.mlp = dim, heads, mlp
+        self.linear1 = torch.nn.Linear(dim, 3 * dim + mlp)
+        self.linear2 = torch.nn.Linear(dim + mlp, dim)
+        self.norm = _QKNorm(dim // heads)
+        self.pre_norm = torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6)
+        self.act = torch.nn.GELU(approximate="tanh")
+        self.modulation = _Modulation(dim, False)
+
+    def forward(self, x, vec, pe):
+        shift, scale, gate = self.modulation(vec)
+        xm = torch.addcmul(shift, self.pre_norm(x), 1 + scale)
+        qkv, mlp = torch.split(self.linear1(xm), [3 * self.dim, self.mlp], dim=-1)
+        q, k, v = _split_heads(qkv, self.heads)
+        q, k = self.norm(q, k, v)
+        a = _attention(q, k, v, pe)
+        return torch.addcmul(x, gate, self.linear2(torch.cat([a, self.act(mlp)], dim=2)))
+
+
+class _MLPEmbedder(torch.nn.Module):
+    def __init__(self, din, dim):
+        super().__init__()
+        self.in_layer, self.out_layer = torch.nn.Linear(din, dim), torch.nn.Linear(dim, dim)
+
+    def forward(self, x):
+        return self.out_layer(torch.nn.functional.silu(self.in_layer(x)))
+
+
+class FluxDiT(torch.nn.Module):
+    """FLUX.1-dev architecture (flow-matching DiT), random init, for BASELINE config 4."""
+
+    def __init__(self, cfg=FLUX_DEV):
+        super().__init__()
+        d, h = cfg["hidden"], cfg["heads"]
+        mlp = int(d * cfg["mlp_ratio"])
+        self.cfg = cfg
+        self.img_in = torch.nn.Linear(cfg["in_channels"], d)
+        self.time_in = _MLPEmbedder(256, d)
+        self.guidance_in = _MLPEmbedder(256, d)
+        self.vector_in = _MLPEmbedder(cfg["vec"], d)
+        self.txt_in = torch.nn.Linear(cfg["context"], d)
+        self.double_blocks = torch.nn.ModuleList([_DoubleBlock(d, h, mlp) for _ in range(cfg["depth"])])
+        self.single_blocks = torch.nn.ModuleList([_SingleBlock(d, h, mlp) for _ in range(cfg["depth_single"])])
+        self.final_norm = torch.nn.LayerNorm(d, elementwise_affine=False, eps=1e-6)
+        self.final_adaln = torch.nn.Linear(d, 2 * d)
+        self.final_linear = torch.nn.Linear(d, cfg["in_channels"])
+
+    def pe(self, ids):
+        return torch.cat([_rope(ids[..., i], a, self.cfg["theta"]) for i, a in enumerate(self.cfg["axes"])],
+                         dim=-3).unsqueeze(1)
+
+    def forward(self, img, txt, pe, t, y, guidance):
+        img = self.img_in(img)
+        vec = self.time_in(_timestep_embedding(t).to(img.dtype))
+        vec = vec + self.guidance_in(_timestep_embedding(guidance).to(img.dtype))
+        vec = vec + self.vector_in(y)
+        txt = self.txt_in(txt)
+        for blk in self.double_blocks:
+            img, txt = blk(img, txt, vec, pe)
+        x = torch.cat([txt, img], dim=1)
+        for blk in self.single_blocks:
+            x = blk(x, vec, pe)
+        x = x[:, txt.shape[1]:]
+        shift, scale = self.final_adaln(torch.nn.functional.silu(vec)).chunk(2, dim=1)
+        x = torch.addcmul(shift[:, None], self.final_norm(x), 1 + scale[:, None])
+        return self.final_linear(x)
+
+
+def build_flux_dit(device, seed, cfg=FLUX_DEV):
+    """Random-init FLUX DiT in bf16: linears W ~ N(0, 0.02), bias ~ N(0, 0.01)."""
+
+    with torch.device(device):
+        model = FluxDiT(cfg)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for m in model.modules():
+            if isinstance(m, torch.nn.Linear):
+                m.weight.normal_(0.0, 0.02, generator=g)
+                if m.bias is not None:
+                    m.bias.normal_(0.0, 0.01, generator=g)
+    return model.to(torch.bfloat16).eval()
+
+
+def dit_inputs(batch, device, seed, cfg=FLUX_DEV, img_tokens=1024, txt_tokens=512):
+    g = torch.Generator(device=device).manual_seed(seed)
+    side = int(round(img_tokens ** 0.5))
+    img = torch.randn((batch, img_tokens, cfg["in_channels"]), generator=g, device=device).to(torch.bfloat16)
+    txt = torch.randn((batch, txt_tokens, cfg["context"]), generator=g, device=device).to(torch.bfloat16)
+    y = torch.randn((batch, cfg["vec"]), generator=g, device=device).to(torch.bfloat16)
+    img_ids = torch.zeros((batch, img_tokens, 3), device=device)
+    img_ids[..., 1] = torch.arange(side, device=device)[:, None].expand(side, side).reshape(-1)
+    img_ids[..., 2] = torch.arange(side, device=device)[None, :].expand(side, side).reshape(-1)
+    ids = torch.cat([torch.zeros((batch, txt_tokens, 3), device=device), img_ids], dim=1)
+    return img, txt, y, ids
+
+
+def run_dit(args, rank, world, local):
+    """20 denoise steps of the FLUX DiT on 1024 image + 512
+    text tokens, batch 8 split data-parallel over the ranks (no collective),
+    dense bf16 and with every eligible linear swapped for ConvRotLinear
+    (mpp-w4a4, g256).  One denoise step (forward + Euler update) is captured
+    as a CUDA graph; the 20-step loop is timed with CUDA events, max over
+    ranks."""
+
+    from convrot_mlx_b200 import _lib
+    from convrot_mlx_b200.adapter import replace_convrot_linears
+
+    device = torch.device("cuda", local if world > 1 else 0)
+    total_batch, steps_per_gen = 8, 20
+    if total_batch % world:
+        raise SystemExit(f"batch {total_batch} does not split over {world} GPUs")
+    b = total_batch // world
+    model = build_flux_dit(device, SEED)
+    img, txt, y, ids = dit_inputs(b, device, SEED + 7 + rank)
+    with torch.no_grad():
+        pe = model.pe(ids)
+    guidance = torch.full((b,), 3.5, device=device)
+    ts = torch.linspace(1.0, 0.0, steps_per_gen + 1, device=device)
+    t_cur, t_next = torch.zeros((b,), device=device), torch.zeros((b,), device=device)
+    x = img.clone()
+
+    def denoise_step():
+        v = model(x, txt, pe, t_cur, y, guidance)
+        x.add_((t_next - t_cur)[:, None, None].to(x.dtype) * v)
+
+    def generation_ms(reps):
+        stream = torch.cuda.Stream(device=device)
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(2):
+                denoise_step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.no_grad(), torch.cuda.graph(graph, stream=stream):
+            denoise_step()
+
+        def generation():
+            x.copy_(img)
+            for i in range(steps_per_gen):
+                t_cur.fill_(float(ts[i]))
+                t_next.fill_(float(ts[i + 1]))
+                graph.replay()
+
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                generation()
+        torch.cuda.synchronize()
+        barrier(world)
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                generation()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        del graph
+        return ms
+
+    dense_ms = generation_ms(args.steps)
+    replaced = replace_convrot_linears(model, backend="mpp-w4a4")
+    torch.cuda.empty_cache()
+    with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
+        w4_ms = generation_ms(args.steps)
+    d = FLUX_DEV["hidden"]
+    mlp = int(d * FLUX_DEV["mlp_ratio"])
+    per_sample = (FLUX_DEV["depth"] * 2 * (1024 + 512) * d * (3 * d + d + 2 * mlp)
+                  + FLUX_DEV["depth_single"] * 2 * 1536 * (d * (3 * d + mlp) + (d + mlp) * d))
+    linear_ops = per_sample * total_batch * steps_per_gen
+    return {
+        "metric": "FLUX DiT 20-step generation latency, batch 8 split over the GPUs (BASELINE config 4)",
+        "value": round(w4_ms, 2), "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(w4_ms / steps_per_gen, 3), "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "W4A4 int8 tensor (eligible linears), bf16 elsewhere",
+        "data": "synthetic, seeded: random-init FLUX.1-dev architecture, W ~ N(0, 0.02), latents/text/vector ~ N(0, 1)",
+        "config": {"workload": "flux-dit (BASELINE config 4)", "batch": total_batch, "per_gpu_batch": b,
+                   "tokens": "1024 image + 512 text", "denoise_steps": steps_per_gen,
+                   "parallelism": f"dp{world} (batch split, no collective)", "linears_w4a4": len(replaced),
+                   "timing": "one denoise step as a CUDA graph, 20 replays per generation, CUDA events, max over ranks"},
+        "dense_bf16_ms": round(dense_ms, 2), "speedup_vs_dense_bf16": round(dense_ms / w4_ms, 3),
+        "linear_tops": round(linear_ops / (w4_ms * 1e-3) / 1e12, 1),
+        "clocks": dict(clocks.summary(), window="nvidia-smi samples during the timed W4A4 generations"),
+        "device_error": _lib.take_device_error(),
+    }
+
+
 VIDEO_M = 32760
 VIDEO_KN = ((5120, 15360), (5120, 13824), (13824, 5120))
 
@@ -695,8 +1006,9 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", choices=("flux-sweep", "video-tp"), default="flux-sweep",
-                    help="flux-sweep: BASELINE config 3 (default); video-tp: config 5, tensor-parallel over --gpus")
+    ap.add_argument("--workload", choices=("flux-sweep", "video-tp", "dit"), default="flux-sweep",
+                    help="flux-sweep: BASELINE config 3 (default); video-tp: config 5, tensor-parallel over --gpus; "
+                         "dit: config 4, FLUX DiT with the batch split over --gpus")
     ap.add_argument("--case", choices=("gemm", "prep"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=3072)
@@ -717,8 +1029,12 @@ def main(argv=None):
         return 0
     rank, world, local = dist_setup(args.gpus)
     try:
-        line = run_video_tp(args, rank, world, local) if args.workload == "video-tp" else run_ours(args, rank, world,
-                                                                                                   local)
+        if args.workload == "video-tp":
+            line = run_video_tp(args, rank, world, local)
+        elif args.workload == "dit":
+            line = run_dit(args, rank, world, local)
+        else:
+            line = run_ours(args, rank, world, local)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:

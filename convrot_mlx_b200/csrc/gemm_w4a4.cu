@@ -22,6 +22,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -213,11 +214,17 @@ __device__ __forceinline__ void store16(float* dst, const float (&v)[32], int o)
     reinterpret_cast<float4*>(dst)[q] = make_float4(v[o + 4 * q], v[o + 4 * q + 1], v[o + 4 * q + 2], v[o + 4 * q + 3]);
 }
 
+// Two outputs rounded to nearest even (as cvt_out) in one paired conversion,
+// a in the low half.
 template <typename T16>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
-  const T16 lo = cvt_out<T16>(a), hi = cvt_out<T16>(b);
-  return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&lo)) |
-         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&hi)) << 16);
+  if constexpr (std::is_same<T16, __nv_bfloat16>::value) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  }
 }
 
 template <typename T16>
@@ -480,6 +487,39 @@ __global__ void __launch_bounds__(kThreads, 1)
 // weight bytes and the transform work of the one-CTA kernel for the same
 // tensor-core rate, and every operand arrives by TMA.
 // ===========================================================================
+// W4A4 epilogue of one 32-column chunk: v[j] = fl(fl(fl(dot_j) * xs) * ws_j)
+// + bias_j (core.py:932-936).  The accumulator holds 16 * dot exactly.  With
+// kDiv16 the caller passes xs / 16, exact because it is still a normal float
+// (or zero, infinite, NaN): then fl(float(acc) * xs / 16) == fl(fl(dot) * xs)
+// -- float(acc) = 16 * fl(dot) and the power-of-two factor cancels exactly --
+// and the shift is saved.  The two products are paired fp32 multiplies
+// (mul2_rn, rounded per component as __fmul_rn); the bias add stays scalar
+// __fadd_rn, because a paired add right after a paired multiply was fused
+// into one rounding by the compiler even with .rn spelled out.
+template <bool kDiv16>
+__device__ __forceinline__ void scale_chunk_i8(const uint32_t (&r)[32], const float* ws, const float* bias, float xs,
+                                               float (&v)[32]) {
+  const float2 xs2 = make_float2(xs, xs);
+#pragma unroll
+  for (int j = 0; j < 32; j += 4) {
+    const float4 w4 = *reinterpret_cast<const float4*>(ws + j);
+    const float4 b4 = *reinterpret_cast<const float4*>(bias + j);
+    float2 d[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int32_t a0 = static_cast<int32_t>(r[j + 2 * h]), a1 = static_cast<int32_t>(r[j + 2 * h + 1]);
+      d[h] = kDiv16 ? make_float2(__int2float_rn(a0), __int2float_rn(a1))
+                    : make_float2(__int2float_rn(a0 >> 4), __int2float_rn(a1 >> 4));
+    }
+    const float2 p0 = mul2_rn(mul2_rn(d[0], xs2), make_float2(w4.x, w4.y));
+    const float2 p1 = mul2_rn(mul2_rn(d[1], xs2), make_float2(w4.z, w4.w));
+    v[j] = __fadd_rn(p0.x, b4.x);
+    v[j + 1] = __fadd_rn(p0.y, b4.y);
+    v[j + 2] = __fadd_rn(p1.x, b4.z);
+    v[j + 3] = __fadd_rn(p1.y, b4.w);
+  }
+}
+
 namespace pair {
 
 constexpr int BM = 256;          // rows per pair tile (128 per CTA)
@@ -637,6 +677,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialized before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // Everything above touches only shared memory, TMEM and kernel parameters,
+  // so it overlaps the previous kernel's tail; global memory comes after.
+  grid_dependency_wait();
+  grid_dependents_launch();
 
   if (warp == kWarpA) {
     // Lane s issues the copies of slot s: copies issued by one thread are
@@ -871,12 +915,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         sws[j] = col < p.N ? __ldg(p.wscales + col) : 0.0f;
         sbias[j] = (col < p.N && p.bias) ? __ldg(p.bias + col) : 0.0f;
       }
+      const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
+      const bool row_ok = m < p.M;
+      // the row scale is loaded before the wait, off the tile's critical path
+      const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
+      const bool xs_div16 = __all_sync(0xFFFFFFFFu, !(fabsf(xs) < 0x1p-122f) || xs == 0.0f);  // xs / 16 exact
       __syncwarp();
       if (!wait(&bars->acc_full[buf], (local >> 1) & 1, bars, 19)) break;
       tc_fence_after();
-      const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
-      const bool row_ok = m < p.M;
-      const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
       const bool gather = p.n_outs > 0;
       const int64_t ldc = gather ? p.ldc : p.N;
       const int64_t row_off = static_cast<int64_t>(row_ok ? m : 0) * ldc + (gather ? p.col_off : 0);
@@ -891,22 +937,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_32x32b_x32(t_row + c * 32, r);
         tmem_ld_wait();
         float v[32];
+        if constexpr (KIND == KIND_I8) {
+          if (xs_div16) scale_chunk_i8<true>(r, sws + c * 32, sbias + c * 32, xs * 0.0625f, v);
+          else scale_chunk_i8<false>(r, sws + c * 32, sbias + c * 32, xs, v);
+        } else {
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
-          const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
-          const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
-          const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if constexpr (KIND == KIND_I8) {
-              // core.py:932-936: fl(fl(fl(dot) * xs) * ws) + bias
-              const float dot = static_cast<float>(static_cast<int32_t>(r[j + u]) >> 4);
-              v[j + u] = __fadd_rn(__fmul_rn(__fmul_rn(dot, xs), wv[u]), bv[u]);
-            } else {
-              // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
-              v[j + u] = __fadd_rn(__fmul_rn(__uint_as_float(r[j + u]), wv[u]), bv[u]);
-            }
+          for (int j = 0; j < 32; j += 4) {  // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
+            const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
+            const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
+            const float2 p0 = mul2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), make_float2(w4.x, w4.y));
+            const float2 p1 = mul2_rn(make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), make_float2(w4.z, w4.w));
+            v[j] = __fadd_rn(p0.x, b4.x);  // scalar add: see scale_chunk_i8
+            v[j + 1] = __fadd_rn(p0.y, b4.y);
+            v[j + 2] = __fadd_rn(p1.x, b4.z);
+            v[j + 3] = __fadd_rn(p1.y, b4.w);
           }
         }
         if constexpr (sizeof(TOut) == 2) {
@@ -1100,13 +1144,15 @@ static int launch_pair(const void* act, const Params& p0, cudaStream_t stream) {
   cfg.blockDim = dim3(pair::kThreads, 1, 1);
   cfg.dynamicSmemBytes = pair::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see grid_dependency_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, p));
   return check_launch("w4a4 pair gemm");
 }

@@ -117,6 +117,27 @@ def test_integer_accumulator_extremes():
     np.testing.assert_array_equal(host(out), O.integer_dot(a, w).astype(np.float32))
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_tiny_and_special_row_scales_exact(out_dtype):
+    # The epilogue multiplies the accumulator (16 * dot) by xs / 16 when every
+    # row scale of a warp keeps xs / 16 exact, and shifts first otherwise.
+    # Rows 0-31 (one epilogue warp) hold scales where xs / 16 is not exact
+    # (subnormal results, subnormal xs) or special (0, inf); rows 32-63 are
+    # ordinary.  Both forms must match the oracle bit for bit.
+    m, n, k = 64, 256, 256
+    a, w, xs, ws, b = _random_case(m, n, k, seed=4242)
+    special = [0.0, 1e-45, 1e-40, 2.0 ** -126, 2.0 ** -123, 2.0 ** -122 * 1.5, 2.0 ** -121, 1e-30, np.inf, 3.0e38]
+    xs[: len(special)] = np.array(special, np.float32)
+    xs[len(special):32] = np.float32(2.0 ** -124)
+    names = {torch.bfloat16: "bfloat16", torch.float32: "float32"}
+    with np.errstate(over="ignore", invalid="ignore"):
+        expected = O.w4a4_epilogue(O.integer_dot(a, w), xs, ws, b, names[out_dtype])
+    out = cr.mpp_w4a4_int8_matmul(cuda(a), cuda(O.pack_signed_int4(w.T.copy())), cuda(xs), cuda(ws), cuda(b),
+                                  output_dtype=out_dtype)
+    np.testing.assert_array_equal(host(out.float()), expected)
+    assert_no_device_error()
+
+
 @pytest.mark.parametrize("m,k,n", [(1536, 3072, 3072), (4096, 3072, 12288), (4096, 15360, 3072)])
 def test_flux_shapes_integer_exact(m, k, n):
     # BASELINE config 3 shapes: the int32 dots must equal an exact reference.

@@ -30,7 +30,11 @@ enum PrepMode : int { kModeI8 = 0, kModePacked = 1, kModeRotate = 2 };
 // Word index of pair-element p in shared memory: rows of 32 words, 16-byte
 // chunks XOR-swizzled so that the row-wise (phase 1 / quantize) and the
 // column-wise (phases 2 and 3) accesses are all free of bank conflicts.
-__device__ __forceinline__ int swz(int p) {
+// swz(p) = p ^ (h(p) << 2) with h made of bit selections and XORs, so swz is
+// linear over XOR: swz(a ^ b) == swz(a) ^ swz(b).  Every access below is a
+// per-thread base plus a loop offset on disjoint bits (so + is ^), and its
+// index is the thread's swizzled base XOR a compile-time constant.
+__host__ __device__ constexpr int swz(int p) {
   const int r = p >> 5;
   const int h = (r & 3) | ((((r >> 1) ^ (r >> 3)) & 1) << 2);
   return (r << 5) | ((((p >> 2) & 7) ^ h) << 2) | (p & 3);
@@ -61,9 +65,10 @@ __device__ __forceinline__ void bfly4(P& a, P& b, P& c, P& d) {
   d = o3;
 }
 
+// 16-byte chunk at swizzled word index s (a multiple of 4).
 template <typename P>
-__device__ __forceinline__ void st_chunk(P* sm, int p, const P& v0, const P& v1, const P& v2, const P& v3) {
-  P* dst = sm + swz(p);
+__device__ __forceinline__ void st_chunk(P* sm, int s, const P& v0, const P& v1, const P& v2, const P& v3) {
+  P* dst = sm + s;
   if constexpr (sizeof(P) == 4) {
     uint4 u;
     u.x = *reinterpret_cast<const uint32_t*>(&v0);
@@ -80,8 +85,8 @@ __device__ __forceinline__ void st_chunk(P* sm, int p, const P& v0, const P& v1,
 }
 
 template <typename P>
-__device__ __forceinline__ void ld_chunk(const P* sm, int p, P& v0, P& v1, P& v2, P& v3) {
-  const P* src = sm + swz(p);
+__device__ __forceinline__ void ld_chunk(const P* sm, int s, P& v0, P& v1, P& v2, P& v3) {
+  const P* src = sm + s;
   if constexpr (sizeof(P) == 4) {
     const uint4 u = *reinterpret_cast<const uint4*>(src);
     v0 = *reinterpret_cast<const P*>(&u.x);
@@ -289,6 +294,19 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
   constexpr bool kExact = !kFast;
   const P nrm = E::splat(kNorm);
 
+  // swizzled bases of this thread's accesses, the same for every row
+  int s_unit[UPT], s_col[UPT], s_col3[UPT];
+#pragma unroll
+  for (int j = 0; j < UPT; ++j) {
+    const int t = tid + j * nthr;
+    s_unit[j] = swz(t << 4);                                // phase 1 and quantize: ^ swz(4m)
+    s_col[j] = G == 64 ? swz(64 * (t >> 2) + 4 * (t & 3))   // phase 2, G = 64: ^ swz(16i)
+                       : swz(256 * (t >> 4) + (t & 15));    // phase 2, G >= 256: ^ swz(16i)
+    s_col3[j] = swz(1024 * (t >> 6) + ((t & 63) << 2));     // phase 3: ^ swz(256i)
+  }
+  grid_dependency_wait();  // the input may come from the previous kernel of the stream
+  grid_dependents_launch();
+
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const T* xr = x + row * static_cast<int64_t>(K);
     float amax = 0.0f;
@@ -328,7 +346,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
         } else {
           const int p0 = u << 4;
 #pragma unroll
-          for (int m = 0; m < 4; ++m) st_chunk(sm, p0 + 4 * m, v[j][4 * m], v[j][4 * m + 1], v[j][4 * m + 2], v[j][4 * m + 3]);
+          for (int m = 0; m < 4; ++m) st_chunk(sm, s_unit[j] ^ swz(4 * m), v[j][4 * m], v[j][4 * m + 1], v[j][4 * m + 2], v[j][4 * m + 3]);
         }
       }
     }
@@ -342,23 +360,20 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
         if (t >= units) continue;
         P w[16];
         if constexpr (G == 64) {
-          const int q = t >> 2, k = t & 3;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) ld_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) ld_chunk(sm, s_col[j] ^ swz(16 * i), w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 #pragma unroll
           for (int c = 0; c < 4; ++c) bfly4<E, kExact>(w[c], w[4 + c], w[8 + c], w[12 + c]);
           finish(w);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) st_chunk(sm, 64 * q + 16 * i + 4 * k, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) st_chunk(sm, s_col[j] ^ swz(16 * i), w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         } else {
-          const int b = t >> 4, c = t & 15;
-          const int base = 256 * b + c;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = sm[swz(base + 16 * i)];
+          for (int i = 0; i < 16; ++i) w[i] = sm[s_col[j] ^ swz(16 * i)];
           stages_1_4<E, 16, kExact>(w);
           if constexpr (G == 256) finish(w);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) sm[swz(base + 16 * i)] = w[i];
+          for (int i = 0; i < 16; ++i) sm[s_col[j] ^ swz(16 * i)] = w[i];
         }
       }
       if constexpr (G == 1024) {
@@ -368,14 +383,13 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
           const int t = tid + j * nthr;
           if (t >= units) continue;
           P w[16];
-          const int q = t >> 6, c0 = (t & 63) << 2;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) ld_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) ld_chunk(sm, s_col3[j] ^ swz(256 * i), w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
 #pragma unroll
           for (int c = 0; c < 4; ++c) bfly4<E, kExact>(w[c], w[4 + c], w[8 + c], w[12 + c]);
           finish(w);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) st_chunk(sm, 1024 * q + c0 + 256 * i, w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) st_chunk(sm, s_col3[j] ^ swz(256 * i), w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
         }
       }
     }
@@ -416,7 +430,7 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
       if constexpr (kSmem) {
         P w[16];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) ld_chunk(sm, p0 + 4 * m, w[4 * m], w[4 * m + 1], w[4 * m + 2], w[4 * m + 3]);
+        for (int m = 0; m < 4; ++m) ld_chunk(sm, s_unit[j] ^ swz(4 * m), w[4 * m], w[4 * m + 1], w[4 * m + 2], w[4 * m + 3]);
         if constexpr (kFast) emit_unit_bf16<MODE>(out, row, K, half, p0, w, rscale);
         else emit_unit<E, T, MODE>(out, row, K, half, p0, w, scale);
       } else {
@@ -445,7 +459,17 @@ static int launch_g(const void* x, int64_t rows, int K, int half, void* out, flo
   const unsigned grid = static_cast<unsigned>(rows < 2147483647LL ? rows : 2147483647LL);
   auto run = [&](auto kernel) -> int {
     if (smem > 48 * 1024) CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    kernel<<<grid, threads, smem, stream>>>(static_cast<const T*>(x), rows, K, half, out, scales);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see grid_dependency_wait
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), rows, K, half, out, scales));
     return check_launch("convrot prep kernel");
   };
   switch (upt) {

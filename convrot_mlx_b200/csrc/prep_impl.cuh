@@ -218,7 +218,8 @@ __device__ __forceinline__ uint32_t codes2_bf16(__nv_bfloat162 v, float r) {
   const uint32_t bits = *reinterpret_cast<const uint32_t*>(&v);
   const float x0 = __uint_as_float(bits << 16);
   const float x1 = __uint_as_float(bits & 0xFFFF0000u);
-  const __nv_bfloat162 q = __floats2bfloat162_rn(__fmul_rn(x0, r), __fmul_rn(x1, r));
+  const float2 xr = mul2_rn(make_float2(x0, x1), make_float2(r, r));  // paired, rounded as __fmul_rn
+  const __nv_bfloat162 q = __floats2bfloat162_rn(xr.x, xr.y);
   const __nv_bfloat162 t = __hadd2(q, __float2bfloat162_rn(136.0f));
   return *reinterpret_cast<const uint32_t*>(&t);
 }
@@ -352,7 +353,11 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
     }
 
     if constexpr (kSmem) {
-      __syncthreads();
+      // Phase 2 works within blocks of 64 (G = 64) or 256 pair-words, whose
+      // units and column tasks both belong to one quarter- or half-warp (task
+      // and unit indices coincide, and the thread count is a multiple of 32),
+      // so a warp barrier orders phase 1's stores before phase 2's loads.
+      __syncwarp();
       // phase 2
 #pragma unroll
       for (int j = 0; j < UPT; ++j) {
@@ -400,20 +405,17 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
         // |x| of the unnormalized rotation; x / sqrt(G) is an exact power-of-two scale
         amax = fmaxf(__low2float(amax2), __high2float(amax2)) * kNorm;
       }
-      // row absmax: warp shuffle, then across warps
+      // row absmax: warp shuffle, one barrier, then every warp reduces the
+      // per-warp maxima itself
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
       if ((tid & 31) == 0) red[tid >> 5] = amax;
       __syncthreads();
-      if (tid < 32) {
-        float m = tid < (nthr >> 5) ? red[tid] : 0.0f;
+      float rmax = (tid & 31) < (nthr >> 5) ? red[tid & 31] : 0.0f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-        if (tid == 0) red[0] = m;
-      }
-      __syncthreads();
+      for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xFFFFFFFFu, rmax, o));
       const float floor_v = E::to_f(E::from_f(1.0e-10f));
-      const float maximum = E::to_f(E::from_f(fmaxf(red[0], floor_v)));
+      const float maximum = E::to_f(E::from_f(fmaxf(rmax, floor_v)));
       scale = E::to_f(E::from_f(__fdiv_rn(maximum, 7.0f)));
       rscale = __fdiv_rn(1.0f, scale) * kNorm;
       if (tid == 0) scales[row] = scale;

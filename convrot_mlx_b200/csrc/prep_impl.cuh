@@ -115,6 +115,13 @@ __device__ __forceinline__ void load16(Raw16<T>& r, const T* src) {
 }
 
 template <typename T>
+__device__ __forceinline__ void load16_shared(Raw16<T>& r, const T* src) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < Raw16<T>::kVec; ++i) r.v[i] = s[i];
+}
+
+template <typename T>
 __device__ __forceinline__ void zero16(Raw16<T>& r) {
 #pragma unroll
   for (int i = 0; i < Raw16<T>::kVec; ++i) r.v[i] = make_uint4(0, 0, 0, 0);
@@ -277,20 +284,32 @@ __device__ __forceinline__ void emit_unit(void* out, int64_t row, int64_t K, int
   if (p0 + half < K) write_half<E, T, MODE>(out, row, K, p0 + half, hi, scale);
 }
 
-template <typename T, int G, int MODE, int UPT>
+// STAGED: the grid is persistent (as many CTAs as are resident; a CTA takes
+// rows blockIdx.x, + gridDim.x, ...) and each row arrives in shared memory by
+// one bulk copy, issued by thread 0 as soon as every thread has read the
+// previous row's raw words (right after the row's one CTA barrier), so the
+// copy overlaps the rest of the row.  The raw words then cost no registers:
+// about twice the rows per SM are in flight than when every thread holds its
+// raw words in registers (the unstaged form, for rows too long to stage).
+template <typename T, int G, int MODE, int UPT, bool STAGED>
 __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int64_t rows, int K, int half,
-                                                     void* __restrict__ out, float* __restrict__ scales) {
+                                                     void* __restrict__ out, float* __restrict__ scales,
+                                                     int* __restrict__ err) {
   using E = Elem<T>;
   using P = typename E::Pair;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr bool kSmem = G >= 64;  // later stages need other threads' words
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   P* sm = reinterpret_cast<P*>(smem_raw);
-  __shared__ float red[32];
+  // raw row (STAGED) after the pair-words; half * sizeof(P) is a multiple of 64
+  T* raw = reinterpret_cast<T*>(smem_raw + (kSmem ? static_cast<size_t>(half) * sizeof(P) : 0));
+  __shared__ float red[2][32];  // per-warp maxima, double-buffered by row parity
+  __shared__ __align__(8) uint64_t raw_full;
+  __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
   const int nthr = blockDim.x;
   const int units = half >> 4;
   constexpr float kNorm = G == 1 ? 1.0f : G == 4 ? 0.5f : G == 16 ? 0.25f : G == 64 ? 0.125f : G == 256 ? 0.0625f : 0.03125f;
-  constexpr bool kSmem = G >= 64;  // later stages need other threads' words
   constexpr bool kFast = kFastQuant<T, MODE>;
   constexpr bool kExact = !kFast;
   const P nrm = E::splat(kNorm);
@@ -305,11 +324,45 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
                        : swz(256 * (t >> 4) + (t & 15));    // phase 2, G >= 256: ^ swz(16i)
     s_col3[j] = swz(1024 * (t >> 6) + ((t & 63) << 2));     // phase 3: ^ swz(256i)
   }
+  const uint32_t row_bytes = static_cast<uint32_t>(K) * sizeof(T);
+  if constexpr (STAGED) {
+    if (tid == 0) {
+      mbar_init(&raw_full, 1);
+      abort_flag = 0;
+      fence_mbar_init();
+    }
+    __syncthreads();
+  }
   grid_dependency_wait();  // the input may come from the previous kernel of the stream
   grid_dependents_launch();
+  if constexpr (STAGED) {
+    if (tid == 0 && static_cast<int64_t>(blockIdx.x) < rows) {
+      mbar_arrive_expect_tx(&raw_full, row_bytes);
+      bulk_load_1d(raw, x + static_cast<int64_t>(blockIdx.x) * K, row_bytes, &raw_full);
+    }
+  }
 
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+  uint32_t iter = 0;
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x, ++iter) {
     const T* xr = x + row * static_cast<int64_t>(K);
+    if constexpr (STAGED) {
+      // Bounded wait for this row's copy (1 s).  On time-out the flag is
+      // raised and the CTA runs its remaining rows through every barrier
+      // without copies or stores, so no thread is left waiting.
+      if (!abort_flag) {
+        const uint64_t t0 = globaltimer();
+        for (uint32_t i = 0;; ++i) {
+          if (mbar_try_wait(&raw_full, iter & 1)) break;
+          if ((i & 255) == 255) {
+            if (*reinterpret_cast<volatile int*>(&abort_flag)) break;
+            if (globaltimer() - t0 > 1000000000ull) {
+              atomicExch(&abort_flag, 1);
+              break;
+            }
+          }
+        }
+      }
+    }
     float amax = 0.0f;
     P amax2 = E::splat(0.0f);  // fast path: packed running max of |x|
     // last-stage bookkeeping: normalize + absmax (generic) or packed absmax (fast)
@@ -323,16 +376,20 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
       }
     };
 
-    // phase 1: issue every load of this thread first, then rotate.
+    // phase 1: unstaged, every global load of this thread first, then
+    // rotate; staged, each unit's raw words come from shared memory just
+    // before it is rotated (few registers live at a time).
     Raw16<T> rlo[UPT], rhi[UPT];
+    if constexpr (!STAGED) {
 #pragma unroll
-    for (int j = 0; j < UPT; ++j) {
-      const int u = tid + j * nthr;
-      if (u < units) {
-        const int p0 = u << 4;
-        load16(rlo[j], xr + p0);
-        if (p0 + half < K) load16(rhi[j], xr + p0 + half);
-        else zero16(rhi[j]);
+      for (int j = 0; j < UPT; ++j) {
+        const int u = tid + j * nthr;
+        if (u < units) {
+          const int p0 = u << 4;
+          load16(rlo[j], xr + p0);
+          if (p0 + half < K) load16(rhi[j], xr + p0 + half);
+          else zero16(rhi[j]);
+        }
       }
     }
     P v[UPT][16];
@@ -340,6 +397,12 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
     for (int j = 0; j < UPT; ++j) {
       const int u = tid + j * nthr;
       if (u < units) {
+        if constexpr (STAGED) {
+          const int p0 = u << 4;
+          load16_shared(rlo[j], raw + p0);
+          if (p0 + half < K) load16_shared(rhi[j], raw + p0 + half);
+          else zero16(rhi[j]);
+        }
         interleave<E>(v[j], rlo[j], rhi[j]);
         stages_1_4<E, G, kExact>(v[j]);
         if constexpr (!kSmem) {
@@ -409,18 +472,31 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
       // per-warp maxima itself
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-      if ((tid & 31) == 0) red[tid >> 5] = amax;
+      if ((tid & 31) == 0) red[iter & 1][tid >> 5] = amax;
       __syncthreads();
-      float rmax = (tid & 31) < (nthr >> 5) ? red[tid & 31] : 0.0f;
+      float rmax = (tid & 31) < (nthr >> 5) ? red[iter & 1][tid & 31] : 0.0f;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xFFFFFFFFu, rmax, o));
       const float floor_v = E::to_f(E::from_f(1.0e-10f));
       const float maximum = E::to_f(E::from_f(fmaxf(rmax, floor_v)));
       scale = E::to_f(E::from_f(__fdiv_rn(maximum, 7.0f)));
       rscale = __fdiv_rn(1.0f, scale) * kNorm;
-      if (tid == 0) scales[row] = scale;
-    } else if constexpr (kSmem) {
+    } else if constexpr (kSmem || STAGED) {
       __syncthreads();
+    }
+    if constexpr (STAGED) {
+      // Every thread has read this row's raw words (they are in registers or
+      // in the pair-word buffer): refill the raw buffer with the next row.
+      // The proxy fence orders those generic reads before the copy's writes.
+      if (tid == 0 && !abort_flag && row + gridDim.x < rows) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(&raw_full, row_bytes);
+        bulk_load_1d(raw, x + (row + gridDim.x) * static_cast<int64_t>(K), row_bytes, &raw_full);
+      }
+      if (abort_flag) continue;  // uniform: raised before the barrier above
+    }
+    if constexpr (MODE != kModeRotate) {
+      if (tid == 0) scales[row] = scale;
     }
 
     // quantize (or emit the rotation)
@@ -440,7 +516,22 @@ __global__ void __launch_bounds__(256) prep_kernel(const T* __restrict__ x, int6
         else emit_unit<E, T, MODE>(out, row, K, half, p0, v[j], scale);
       }
     }
-    if (row + gridDim.x < rows) __syncthreads();  // smem / red reuse by the next row
+    // Reuse by the next row: the raw buffer is refilled only after the next
+    // CTA barrier above; `red` alternates by row parity; the pair-words of a
+    // unit are rewritten by the same quarter- or half-warp that reads them
+    // (ordered by warp barriers), and for G = 1024 only after the next row's
+    // CTA barrier before phase 3.
+    if constexpr (!STAGED) {
+      if (row + gridDim.x < rows) __syncthreads();
+    }
+  }
+  if constexpr (STAGED) {
+    if (tid == 0 && abort_flag) {
+      atomicCAS(err, 0, 41);
+      const uint64_t t0 = globaltimer();  // let a copy still in flight land
+      while (globaltimer() - t0 < 2000000ull) {
+      }
+    }
   }
 }
 
@@ -455,12 +546,28 @@ static int launch_g(const void* x, int64_t rows, int K, int half, void* out, flo
   int threads = ((units + upt - 1) / upt + 31) / 32 * 32;
   CONVROT_REQUIRE(threads <= 256, CONVROT_ERR_UNSUPPORTED, "features %d too large for the fused kernel", K);
   using P = typename Elem<T>::Pair;
-  const size_t smem = G >= 64 ? static_cast<size_t>(half) * sizeof(P) : 0;
-  CONVROT_REQUIRE(smem <= 227 * 1024, CONVROT_ERR_UNSUPPORTED, "features %d too large for the fused kernel", K);
+  const size_t pair_bytes = G >= 64 ? static_cast<size_t>(half) * sizeof(P) : 0;
+  CONVROT_REQUIRE(pair_bytes <= 227 * 1024, CONVROT_ERR_UNSUPPORTED, "features %d too large for the fused kernel", K);
   if (rows == 0) return CONVROT_OK;
-  const unsigned grid = static_cast<unsigned>(rows < 2147483647LL ? rows : 2147483647LL);
+  // Stage rows of 16 KB and more through shared memory (shorter rows fit
+  // enough CTAs per SM unstaged), while pair-words + raw row leave room for at
+  // least two CTAs per SM.
+  const size_t row_bytes = static_cast<size_t>(K) * sizeof(T);
+  const size_t staged_bytes = pair_bytes + row_bytes;
+  const bool staged = row_bytes >= 16 * 1024 && staged_bytes <= 100 * 1024;
+  const size_t smem = staged ? staged_bytes : pair_bytes;
+  int* err = device_error_word();
+  CONVROT_REQUIRE(err != nullptr, CONVROT_ERR_CUDA, "device error word unavailable");
   auto run = [&](auto kernel) -> int {
-    if (smem > 48 * 1024) CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    int64_t grid_rows = rows < 2147483647LL ? rows : 2147483647LL;
+    if (staged) {  // persistent: as many CTAs as are resident at once
+      int per_sm = 0;
+      CONVROT_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem));
+      const int64_t resident = static_cast<int64_t>(per_sm > 0 ? per_sm : 1) * device_sm_count();
+      if (resident < grid_rows) grid_rows = resident;
+    }
+    const unsigned grid = static_cast<unsigned>(grid_rows);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
     cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
@@ -471,14 +578,22 @@ static int launch_g(const void* x, int64_t rows, int K, int half, void* out, flo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), rows, K, half, out, scales));
+    CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), rows, K, half, out, scales, err));
     return check_launch("convrot prep kernel");
   };
+  if (staged) {
+    switch (upt) {
+      case 1: return run(prep_kernel<T, G, MODE, 1, true>);
+      case 2: return run(prep_kernel<T, G, MODE, 2, true>);
+      case 4: return run(prep_kernel<T, G, MODE, 4, true>);
+      default: return run(prep_kernel<T, G, MODE, 8, true>);
+    }
+  }
   switch (upt) {
-    case 1: return run(prep_kernel<T, G, MODE, 1>);
-    case 2: return run(prep_kernel<T, G, MODE, 2>);
-    case 4: return run(prep_kernel<T, G, MODE, 4>);
-    default: return run(prep_kernel<T, G, MODE, 8>);
+    case 1: return run(prep_kernel<T, G, MODE, 1, false>);
+    case 2: return run(prep_kernel<T, G, MODE, 2, false>);
+    case 4: return run(prep_kernel<T, G, MODE, 4, false>);
+    default: return run(prep_kernel<T, G, MODE, 8, false>);
   }
 }
 

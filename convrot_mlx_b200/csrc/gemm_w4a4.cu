@@ -575,6 +575,16 @@ constexpr size_t kSmemBytes =
     1024 + S * (kABytes + kBpBytes) + B8 * kB8Bytes + kEpiBytes + kStageOutBytes + sizeof(Bars);
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
+// Named barriers 1-4: the epilogue warp of TMEM lane quarter q hands the last
+// tile's staged scales to helper warp 4 + q (64 threads each).
+constexpr int kHelpBar0 = 1;
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // Waits use cluster-scope acquire: most barriers of the pair kernel receive
 // arrivals from the other CTA.
 __device__ __noinline__ bool wait(uint64_t* bar, uint32_t parity, Bars* b, int code) {
@@ -681,6 +691,122 @@ __global__ void __launch_bounds__(kThreads, 1)
   // so it overlaps the previous kernel's tail; global memory comes after.
   grid_dependency_wait();
   grid_dependents_launch();
+
+  // Epilogue of one tile for TMEM lane quarter `quarter` (rows quarter * 32 ..
+  // + 31 of this CTA's half), 32-column chunks [c_begin, c_end): waits for
+  // the accumulator, then scales, converts and stores.  sws / sbias: the
+  // tile's column scales and bias; stage_base: this warp's 2 KB of shared
+  // memory for restaging 16-bit outputs.  False when the wait failed.
+  auto epi_chunks = [&](int tile, int local, int quarter, int c_begin, int c_end, const float* sws,
+                        const float* sbias, uint32_t stage_base) -> bool {
+      const int buf = local & 1;
+      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      const int m = m_blk * BM + 128 * rank + quarter * 32 + lane;
+      const bool row_ok = m < p.M;
+      // the row scale is loaded before the wait, off the tile's critical path
+      const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
+      const bool xs_div16 = __all_sync(0xFFFFFFFFu, !(fabsf(xs) < 0x1p-122f) || xs == 0.0f);  // xs / 16 exact
+      __syncwarp();
+      if (!wait(&bars->acc_full[buf], (local >> 1) & 1, bars, 19)) return false;
+      tc_fence_after();
+      const bool gather = p.n_outs > 0;
+      const int64_t ldc = gather ? p.ldc : p.N;
+      const int64_t row_off = static_cast<int64_t>(row_ok ? m : 0) * ldc + (gather ? p.col_off : 0);
+      TOut* orow = static_cast<TOut*>(p.out) + row_off;
+      const bool vec_store = ((gather ? (ldc | p.col_off) : p.N) % (16 / sizeof(TOut))) == 0;
+      const uint32_t t_row = tmem_base + ((static_cast<uint32_t>(quarter) * 32u) << 16) + buf * BN;
+      for (int c = c_begin; c < c_end; ++c) {
+        const int n = n_blk * BN + c * 32;
+        if (n >= p.N) break;  // uniform across the warp
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(t_row + c * 32, r);
+        tmem_ld_wait();
+        float v[32];
+        if constexpr (KIND == KIND_I8) {
+          if (xs_div16) scale_chunk_i8<true>(r, sws + c * 32, sbias + c * 32, xs * 0.0625f, v);
+          else scale_chunk_i8<false>(r, sws + c * 32, sbias + c * 32, xs, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {  // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
+            const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
+            const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
+            const float2 p0 = mul2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), make_float2(w4.x, w4.y));
+            const float2 p1 = mul2_rn(make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), make_float2(w4.z, w4.w));
+            v[j] = __fadd_rn(p0.x, b4.x);  // scalar add: see scale_chunk_i8
+            v[j + 1] = __fadd_rn(p0.y, b4.y);
+            v[j + 2] = __fadd_rn(p1.x, b4.z);
+            v[j + 3] = __fadd_rn(p1.y, b4.w);
+          }
+        }
+        if constexpr (sizeof(TOut) == 2) {
+          if (vec_store && n + 32 <= p.N) {  // warp-uniform; every lane takes part
+            // lane = row would give 32 scattered 16-byte pieces per store
+            // instruction (NVLink carries those badly, L2 merges them at a
+            // cost).  Restage the warp's
+            // 32 x 32 chunk in shared memory (16-byte chunk q of row r at
+            // ((q + r / 2) % 4) -- conflict-free both ways) and store it with
+            // four lanes per row: 64 contiguous bytes per row, 8 rows per
+            // instruction.
+            const uint32_t sb = stage_base;
+            __syncwarp();
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              sts128(sb + lane * 64 + (((q + (lane >> 1)) & 3) << 4), pack2<TOut>(v[8 * q], v[8 * q + 1]),
+                     pack2<TOut>(v[8 * q + 2], v[8 * q + 3]), pack2<TOut>(v[8 * q + 4], v[8 * q + 5]),
+                     pack2<TOut>(v[8 * q + 6], v[8 * q + 7]));
+            __syncwarp();
+            uint4 piece[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int r = i * 8 + (lane >> 2), q = lane & 3;
+              const uint32_t a = sb + r * 64 + (((q + (r >> 1)) & 3) << 4);
+              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(piece[i].x), "=r"(piece[i].y), "=r"(piece[i].z), "=r"(piece[i].w)
+                           : "r"(a));
+            }
+            const int64_t row0 = static_cast<int64_t>(m_blk * BM + 128 * rank + quarter * 32);
+            const int n_dst = gather ? p.n_outs : 1;
+#pragma unroll 1
+            for (int d = 0; d < n_dst; ++d) {
+              TOut* base = static_cast<TOut*>(gather ? p.outs[d] : p.out) + (gather ? p.col_off : 0) + n +
+                           (lane & 3) * 8;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int64_t r = row0 + i * 8 + (lane >> 2);
+                if (r < p.M) *reinterpret_cast<uint4*>(base + r * ldc) = piece[i];
+              }
+            }
+            continue;
+          }
+        }
+        if (!row_ok) continue;
+        if (gather) {
+          // this tile's columns into every destination (peers over NVLink)
+#pragma unroll 1
+          for (int d = 0; d < p.n_outs; ++d) {
+            TOut* drow = static_cast<TOut*>(p.outs[d]) + row_off;
+            if (vec_store && n + 32 <= p.N) {
+              store16(drow + n, v, 0);
+              store16(drow + n + 16, v, 16);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n + j < p.N) drow[n + j] = cvt_out<TOut>(v[j]);
+            }
+          }
+        } else if (vec_store && n + 32 <= p.N) {
+          store16(orow + n, v, 0);
+          store16(orow + n + 16, v, 16);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n + j < p.N) orow[n + j] = cvt_out<TOut>(v[j]);
+        }
+      }
+      return true;
+  };
+
 
   if (warp == kWarpA) {
     // Lane s issues the copies of slot s: copies issued by one thread are
@@ -905,125 +1031,50 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* sws = epi + ew * 2 * BN;
     float* sbias = sws + BN;
     const uint32_t lead_empty0 = mapa_shared(&bars->acc_empty[0], 0);
+    // this CTA's last tile: columns 128.. go to the helper warp of this quarter
+    const int last_local = pair_id < num_tiles ? (num_tiles - 1 - pair_id) / num_pairs : -1;
+    bool helper_released = false;
     int local = 0;
     for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++local) {
       const int buf = local & 1;
-      const int m_blk = tile % p.m_tiles, n_blk = tile / p.m_tiles;
+      const int n_blk = tile / p.m_tiles;
       __syncwarp();
       for (int j = lane; j < BN; j += 32) {
         const int col = n_blk * BN + j;
         sws[j] = col < p.N ? __ldg(p.wscales + col) : 0.0f;
         sbias[j] = (col < p.N && p.bias) ? __ldg(p.bias + col) : 0.0f;
       }
-      const int m = m_blk * BM + 128 * rank + ew * 32 + lane;
-      const bool row_ok = m < p.M;
-      // the row scale is loaded before the wait, off the tile's critical path
-      const float xs = (KIND == KIND_I8 && row_ok) ? __ldg(p.xscales + m) : 0.0f;
-      const bool xs_div16 = __all_sync(0xFFFFFFFFu, !(fabsf(xs) < 0x1p-122f) || xs == 0.0f);  // xs / 16 exact
       __syncwarp();
-      if (!wait(&bars->acc_full[buf], (local >> 1) & 1, bars, 19)) break;
-      tc_fence_after();
-      const bool gather = p.n_outs > 0;
-      const int64_t ldc = gather ? p.ldc : p.N;
-      const int64_t row_off = static_cast<int64_t>(row_ok ? m : 0) * ldc + (gather ? p.col_off : 0);
-      TOut* orow = static_cast<TOut*>(p.out) + row_off;
-      const bool vec_store = ((gather ? (ldc | p.col_off) : p.N) % (16 / sizeof(TOut))) == 0;
-      const uint32_t t_row = tmem_base + ((ew * 32u) << 16) + buf * BN;
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n = n_blk * BN + c * 32;
-        if (n >= p.N) break;  // uniform across the warp
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld_32x32b_x32(t_row + c * 32, r);
-        tmem_ld_wait();
-        float v[32];
-        if constexpr (KIND == KIND_I8) {
-          if (xs_div16) scale_chunk_i8<true>(r, sws + c * 32, sbias + c * 32, xs * 0.0625f, v);
-          else scale_chunk_i8<false>(r, sws + c * 32, sbias + c * 32, xs, v);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {  // core.py:1145-1152: fl(dots * ws) + bias, fp32 dots
-            const float4 w4 = *reinterpret_cast<const float4*>(sws + c * 32 + j);
-            const float4 b4 = *reinterpret_cast<const float4*>(sbias + c * 32 + j);
-            const float2 p0 = mul2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), make_float2(w4.x, w4.y));
-            const float2 p1 = mul2_rn(make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), make_float2(w4.z, w4.w));
-            v[j] = __fadd_rn(p0.x, b4.x);  // scalar add: see scale_chunk_i8
-            v[j + 1] = __fadd_rn(p0.y, b4.y);
-            v[j + 2] = __fadd_rn(p1.x, b4.z);
-            v[j + 3] = __fadd_rn(p1.y, b4.w);
-          }
-        }
-        if constexpr (sizeof(TOut) == 2) {
-          if (vec_store && n + 32 <= p.N) {  // warp-uniform; every lane takes part
-            // lane = row would give 32 scattered 16-byte pieces per store
-            // instruction (NVLink carries those badly, L2 merges them at a
-            // cost).  Restage the warp's
-            // 32 x 32 chunk in shared memory (16-byte chunk q of row r at
-            // ((q + r / 2) % 4) -- conflict-free both ways) and store it with
-            // four lanes per row: 64 contiguous bytes per row, 8 rows per
-            // instruction.
-            const uint32_t sb = smem_u32(stage_out) + ew * 2048;
-            __syncwarp();
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              sts128(sb + lane * 64 + (((q + (lane >> 1)) & 3) << 4), pack2<TOut>(v[8 * q], v[8 * q + 1]),
-                     pack2<TOut>(v[8 * q + 2], v[8 * q + 3]), pack2<TOut>(v[8 * q + 4], v[8 * q + 5]),
-                     pack2<TOut>(v[8 * q + 6], v[8 * q + 7]));
-            __syncwarp();
-            uint4 piece[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int r = i * 8 + (lane >> 2), q = lane & 3;
-              const uint32_t a = sb + r * 64 + (((q + (r >> 1)) & 3) << 4);
-              asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                           : "=r"(piece[i].x), "=r"(piece[i].y), "=r"(piece[i].z), "=r"(piece[i].w)
-                           : "r"(a));
-            }
-            const int64_t row0 = static_cast<int64_t>(m_blk * BM + 128 * rank + ew * 32);
-            const int n_dst = gather ? p.n_outs : 1;
-#pragma unroll 1
-            for (int d = 0; d < n_dst; ++d) {
-              TOut* base = static_cast<TOut*>(gather ? p.outs[d] : p.out) + (gather ? p.col_off : 0) + n +
-                           (lane & 3) * 8;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int64_t r = row0 + i * 8 + (lane >> 2);
-                if (r < p.M) *reinterpret_cast<uint4*>(base + r * ldc) = piece[i];
-              }
-            }
-            continue;
-          }
-        }
-        if (!row_ok) continue;
-        if (gather) {
-          // this tile's columns into every destination (peers over NVLink)
-#pragma unroll 1
-          for (int d = 0; d < p.n_outs; ++d) {
-            TOut* drow = static_cast<TOut*>(p.outs[d]) + row_off;
-            if (vec_store && n + 32 <= p.N) {
-              store16(drow + n, v, 0);
-              store16(drow + n + 16, v, 16);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n + j < p.N) drow[n + j] = cvt_out<TOut>(v[j]);
-            }
-          }
-        } else if (vec_store && n + 32 <= p.N) {
-          store16(orow + n, v, 0);
-          store16(orow + n + 16, v, 16);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n + j < p.N) orow[n + j] = cvt_out<TOut>(v[j]);
-        }
+      const bool last = local == last_local;
+      if (last) {
+        named_bar_arrive(kHelpBar0 + ew, 64);  // scales staged: the helper may read them
+        helper_released = true;
       }
+      if (!epi_chunks(tile, local, ew, 0, last ? BN / 64 : BN / 32, sws, sbias, smem_u32(stage_out) + ew * 2048))
+        break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(lead_empty0 + buf * 8);
     }
+    // after an error before the last tile: still release the helper (its own
+    // accumulator wait then fails at once on the recorded error)
+    if (!helper_released && last_local >= 0) named_bar_arrive(kHelpBar0 + ew, 64);
     // peers read the gathered output after a flag barrier that follows this
     // kernel: make this thread's stores to their memory visible system-wide
+    if (p.n_outs > 0) __threadfence_system();
+  }
+
+  // Helpers: once their own work is done, warps 4-7 (TMEM lane quarters 0-3)
+  // take columns 128..255 of the CTA's last tile, whose epilogue is otherwise
+  // exposed after the last MMA.  They restage through the int8 weight ring,
+  // idle once the last accumulator is complete.
+  if (warp >= 4 && warp < 8 && pair_id < num_tiles) {
+    const int q = warp & 3;
+    const int last_local = (num_tiles - 1 - pair_id) / num_pairs;
+    named_bar_sync(kHelpBar0 + q, 64);  // the quarter's epilogue warp has staged the scales
+    const float* hws = epi + q * 2 * BN;
+    epi_chunks(pair_id + last_local * num_pairs, last_local, q, BN / 64, BN / 32, hws, hws + BN,
+               smem_u32(sB8) + (warp - 4) * 2048);
     if (p.n_outs > 0) __threadfence_system();
   }
 

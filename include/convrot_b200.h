@@ -201,7 +201,12 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
  * whose wait times out stops early and records a non-zero code in a
  * device-side word.  This reads and clears that word (0 = no time-out).  It
  * synchronizes the current device.  No reference counterpart (the reference
- * has no failure detection beyond shape checks).
+ * has no failure detection beyond shape checks).  Codes (the first recorded
+ * wins): 1-7 one-CTA W4A4 GEMM; 11-19 CTA-pair GEMM (11/12 copy slot free
+ * for A / packed weights, 13 accumulator buffer free, 14 A stage landed,
+ * 15 expanded weights ready, 16 final MMA drain, 17 packed weights landed,
+ * 18 expanded-weight slot free, 19 accumulator ready); 31 peer flag barrier;
+ * 41 staged prep row copy.
  */
 int convrot_take_device_error(int* code);
 

@@ -21,6 +21,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <type_traits>
 
@@ -31,15 +32,19 @@ namespace convrot {
 __device__ int g_convrot_device_error = 0;
 
 int* device_error_word() {
-  static int* words[64] = {};
+  // per-device cache; host threads may race to fill a slot with the same
+  // address, so the slots are atomic
+  static std::atomic<int*> words[64] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (words[dev] == nullptr) {
+  int* w = words[dev].load(std::memory_order_acquire);
+  if (w == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_convrot_device_error) != cudaSuccess) return nullptr;
-    words[dev] = static_cast<int*>(p);
+    w = static_cast<int*>(p);
+    words[dev].store(w, std::memory_order_release);
   }
-  return words[dev];
+  return w;
 }
 
 namespace w4a4 {

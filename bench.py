@@ -488,8 +488,31 @@ def run_e2e(args, shapes, layers, xs_dev, device, world):
     dev_ms = max(e0.elapsed_time(e1), wall * 1e3)
     dev_ms = max_over_ranks(dev_ms, world)
     value = world * total_ops(shapes) * args.steps / (dev_ms * 1e-3) / 1e12
+
+    # the same bytes with no compute: every upload on one stream, every
+    # download (of preallocated device outputs) on another, concurrently
+    dev_out = [torch.empty((m, n), dtype=torch.bfloat16, device=device) for (m, k, n) in shapes]
+    dev_in = [torch.empty_like(x) for x in xs_dev]
+
+    def copies():
+        for hx, dx in zip(host_x, dev_in):
+            with torch.cuda.stream(copy_in):
+                dx.copy_(hx, non_blocking=True)
+        for ho, do in zip(host_out, dev_out):
+            with torch.cuda.stream(copy_out):
+                ho.copy_(do, non_blocking=True)
+
+    copies()
+    torch.cuda.synchronize()
+    c0 = time.perf_counter()
+    for _ in range(args.steps):
+        copies()
+    torch.cuda.synchronize()
+    copy_ms = (time.perf_counter() - c0) * 1e3 / args.steps
+    del dev_out, dev_in
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(dev_ms / args.steps, 3),
+            "copy_only_ms_per_step": round(copy_ms, 3), "frac_of_copy_bound": round(copy_ms / (dev_ms / args.steps), 3),
             "api": "ConvRotLinear.forward (mpp-w4a4) with pinned-host inputs and outputs, copies overlapped on streams"}
 
 
@@ -563,236 +586,86 @@ def run_reference(args, rank, world):
                 "torch-CPU restatement (oracle/torch_cpu.py), with all host threads",
     }
 
+# ---------------------------------------------------------------------------
+# shared timing helper
+
+
+def graph_ms(fn, reps: int, stream, warm: int = 1) -> float:
+    """Capture ``fn`` once as a CUDA graph on ``stream`` and return the mean
+    milliseconds of ``reps`` replays between CUDA events on that stream."""
+
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        fn()
+    with torch.cuda.stream(stream):
+        for _ in range(warm):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / reps
+
 
 # ---------------------------------------------------------------------------
-# a random-init FLUX.1-dev-architecture DiT (the
-# reference runs FLUX through Apple's MLX example, examples/flux1_dev; the
-# model code below is written from the published architecture: 19 double-
-# stream and 38 single-stream blocks, hidden 3072, 24 heads of 128, MLP
-# ratio 4, 3-axis RoPE (16, 56, 56), 64 latent channels, 4096-wide text
-# context, 768-wide pooled vector, guidance embedding).
+# BASELINE config 2: the fused rotate + A4 quantize alone
 
-FLUX_DEV = dict(hidden=3072, heads=24, mlp_ratio=4.0, depth=19, depth_single=38, in_channels=64, context=4096,
-                vec=768, axes=(16, 56, 56), theta=10000)
+C2_M, C2_K = 4096, 3072
 
 
-def _rope(pos, dim, theta):
-    scale = torch.arange(0, dim, 2, dtype=torch.float64, device=pos.device) / dim
-    omega = 1.0 / (theta ** scale)
-    out = pos.to(torch.float64)[..., None] * omega
-    out = torch.stack([torch.cos(out), -torch.sin(out), torch.sin(out), torch.cos(out)], dim=-1)
-    return out.reshape(*out.shape[:-1], 2, 2).float()
+def run_c2(args, device):
+    """Prep-only throughput at BASELINE config 2 (x bf16 4096 x 3072 ~ N(0, 1)
+    with 1% outlier channels x20) for groups 64 and 256, int8 codes out.
+    One CUDA graph launches the kernel over 8 distinct inputs (200 MB of
+    input, > the 126 MB L2), replayed between CUDA events."""
+
+    from convrot_mlx_b200 import _lib
+
+    lib = _lib.load()
+    peaks = load_peaks()
+    n_in = 8
+    xs = [make_activation(C2_M, C2_K, SEED + 300 + i, device) for i in range(n_in)]
+    codes = [torch.empty((C2_M, C2_K), dtype=torch.int8, device=device) for _ in range(n_in)]
+    scales = [torch.empty((C2_M,), dtype=torch.float32, device=device) for _ in range(n_in)]
+    stream = torch.cuda.Stream(device=device)
+    bytes_per_launch = 2 * C2_M * C2_K + C2_M * C2_K + 4 * C2_M
+    out = {"shape": [C2_M, C2_K], "bytes_per_launch": bytes_per_launch, "peak_gbs": peaks["hbm_gbs"],
+           "timing": "graph of 8 launches on 8 distinct inputs (> L2), CUDA events"}
+    for group in (64, 256):
+        def launches(group=group):
+            s = _lib.stream_of(xs[0])
+            for i in range(n_in):
+                _lib.check(lib.convrot_prepare_i8(_lib.ptr(xs[i]), _lib.BF16, C2_M, C2_K, group, _lib.ptr(codes[i]),
+                                                  _lib.ptr(scales[i]), s), "prep")
+
+        ms = graph_ms(launches, max(3, args.steps), stream) / n_in
+        gbs = bytes_per_launch / (ms * 1e-3) / 1e9
+        out[f"g{group}"] = {"us_per_launch": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                            "frac": round(gbs / peaks["hbm_gbs"], 4)}
+    del xs, codes, scales
+    return out
 
 
-def _apply_rope(xq, xk, freqs):
-    xq_ = xq.float().reshape(*xq.shape[:-1], -1, 1, 2)
-    xk_ = xk.float().reshape(*xk.shape[:-1], -1, 1, 2)
-    xq_out = freqs[..., 0] * xq_[..., 0] + freqs[..., 1] * xq_[..., 1]
-    xk_out = freqs[..., 0] * xk_[..., 0] + freqs[..., 1] * xk_[..., 1]
-    return xq_out.reshape(*xq.shape).type_as(xq), xk_out.reshape(*xk.shape).type_as(xk)
+# ---------------------------------------------------------------------------
+# BASELINE config 4: the FLUX DiT, batch 8 split data-parallel (no collective)
 
 
-def _attention(q, k, v, pe):
-    q, k = _apply_rope(q, k, pe)
-    x = torch.nn.functional.scaled_dot_product_attention(q, k, v)
-    b, h, l, d = x.shape
-    return x.transpose(1, 2).reshape(b, l, h * d)
+def run_dit(args, rank, world, local, gens: int, warm_gens: int):
+    """20-step generation latency of the random-init FLUX.1-dev DiT
+    (``flux_dit.py``) on 1024 image + 512 text tokens, batch 8 split over the
+    ranks with no collective: dense bf16, then with every eligible linear
+    swapped for ConvRotLinear (mpp-w4a4, g256) and the modulated norms fused
+    into the activation preparation.  One denoise step (forward + Euler
+    update) is captured as a CUDA graph; a generation is 20 replays, timed
+    with CUDA events, max over ranks."""
 
-
-def _timestep_embedding(t, dim=256, max_period=10000, time_factor=1000.0):
-    import math
-
-    t = time_factor * t
-    half = dim // 2
-    freqs = torch.exp(-math.log(max_period) * torch.arange(half, dtype=torch.float32, device=t.device) / half)
-    args = t[:, None].float() * freqs[None]
-    return torch.cat([torch.cos(args), torch.sin(args)], dim=-1)
-
-
-class _RMSNorm(torch.nn.Module):
-    def __init__(self, dim):
-        super().__init__()
-        self.scale = torch.nn.Parameter(torch.ones(dim))
-
-    def forward(self, x):
-        return torch.nn.functional.rms_norm(x, (x.shape[-1],), self.scale.to(x.dtype), 1e-6)
-
-
-class _QKNorm(torch.nn.Module):
-    def __init__(self, dim):
-        super().__init__()
-        self.query_norm, self.key_norm = _RMSNorm(dim), _RMSNorm(dim)
-
-    def forward(self, q, k, v):
-        return self.query_norm(q).to(v.dtype), self.key_norm(k).to(v.dtype)
-
-
-class _Modulation(torch.nn.Module):
-    def __init__(self, dim, double):
-        super().__init__()
-        self.n = 6 if double else 3
-        self.lin = torch.nn.Linear(dim, self.n * dim)
-
-    def forward(self, vec):
-        return self.lin(torch.nn.functional.silu(vec))[:, None, :].chunk(self.n, dim=-1)
-
-
-class _SelfAttention(torch.nn.Module):
-    def __init__(self, dim, heads):
-        super().__init__()
-        self.heads = heads
-        self.qkv = torch.nn.Linear(dim, 3 * dim, bias=True)
-        self.norm = _QKNorm(dim // heads)
-        self.proj = torch.nn.Linear(dim, dim)
-
-
-def _split_heads(qkv, heads):
-    b, l, _ = qkv.shape
-    q, k, v = qkv.reshape(b, l, 3, heads, -1).permute(2, 0, 3, 1, 4).unbind(0)
-    return q.contiguous(), k.contiguous(), v.contiguous()
-
-
-class _DoubleBlock(torch.nn.Module):
-    def __init__(self, dim, heads, mlp):
-        super().__init__()
-        self.heads = heads
-        for side in ("img", "txt"):
-            setattr(self, f"{side}_mod", _Modulation(dim, True))
-            setattr(self, f"{side}_norm1", torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6))
-            setattr(self, f"{side}_attn", _SelfAttention(dim, heads))
-            setattr(self, f"{side}_norm2", torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6))
-            setattr(self, f"{side}_mlp", torch.nn.Sequential(torch.nn.Linear(dim, mlp), torch.nn.GELU(approximate="tanh"),
-                                                              torch.nn.Linear(mlp, dim)))
-
-    def forward(self, img, txt, vec, pe):
-        im = self.img_mod(vec)
-        tm = self.txt_mod(vec)
-        qkv = []
-        for side, x, m in (("txt", txt, tm), ("img", img, im)):
-            xm = torch.addcmul(m[0], getattr(self, f"{side}_norm1")(x), 1 + m[1])
-            attn = getattr(self, f"{side}_attn")
-            q, k, v = _split_heads(attn.qkv(xm), self.heads)
-            q, k = attn.norm(q, k, v)
-            qkv.append((q, k, v))
-        q = torch.cat([qkv[0][0], qkv[1][0]], dim=2)
-        k = torch.cat([qkv[0][1], qkv[1][1]], dim=2)
-        v = torch.cat([qkv[0][2], qkv[1][2]], dim=2)
-        a = _attention(q, k, v, pe)
-        t_len = txt.shape[1]
-        ta, ia = a[:, :t_len], a[:, t_len:]
-        img = torch.addcmul(img, im[2], self.img_attn.proj(ia))
-        img = torch.addcmul(img, im[5], self.img_mlp(torch.addcmul(im[3], self.img_norm2(img), 1 + im[4])))
-        txt = torch.addcmul(txt, tm[2], self.txt_attn.proj(ta))
-        txt = torch.addcmul(txt, tm[5], self.txt_mlp(torch.addcmul(tm[3], self.txt_norm2(txt), 1 + tm[4])))
-        return img, txt
-
-
-class _SingleBlock(torch.nn.Module):
-    def __init__(self, dim, heads, mlp):
-        super().__init__()
-        self.dim, self.heads, self.mlp = dim, heads, mlp
-        self.linear1 = torch.nn.Linear(dim, 3 * dim + mlp)
-        self.linear2 = torch.nn.Linear(dim + mlp, dim)
-        self.norm = _QKNorm(dim // heads)
-        self.pre_norm = torch.nn.LayerNorm(dim, elementwise_affine=False, eps=1e-6)
-        self.act = torch.nn.GELU(approximate="tanh")
-        self.modulation = _Modulation(dim, False)
-
-    def forward(self, x, vec, pe):
-        shift, scale, gate = self.modulation(vec)
-        xm = torch.addcmul(shift, self.pre_norm(x), 1 + scale)
-        qkv, mlp = torch.split(self.linear1(xm), [3 * self.dim, self.mlp], dim=-1)
-        q, k, v = _split_heads(qkv, self.heads)
-        q, k = self.norm(q, k, v)
-        a = _attention(q, k, v, pe)
-        return torch.addcmul(x, gate, self.linear2(torch.cat([a, self.act(mlp)], dim=2)))
-
-
-class _MLPEmbedder(torch.nn.Module):
-    def __init__(self, din, dim):
-        super().__init__()
-        self.in_layer, self.out_layer = torch.nn.Linear(din, dim), torch.nn.Linear(dim, dim)
-
-    def forward(self, x):
-        return self.out_layer(torch.nn.functional.silu(self.in_layer(x)))
-
-
-class FluxDiT(torch.nn.Module):
-    """FLUX.1-dev architecture (flow-matching DiT), random init, for BASELINE config 4."""
-
-    def __init__(self, cfg=FLUX_DEV):
-        super().__init__()
-        d, h = cfg["hidden"], cfg["heads"]
-        mlp = int(d * cfg["mlp_ratio"])
-        self.cfg = cfg
-        self.img_in = torch.nn.Linear(cfg["in_channels"], d)
-        self.time_in = _MLPEmbedder(256, d)
-        self.guidance_in = _MLPEmbedder(256, d)
-        self.vector_in = _MLPEmbedder(cfg["vec"], d)
-        self.txt_in = torch.nn.Linear(cfg["context"], d)
-        self.double_blocks = torch.nn.ModuleList([_DoubleBlock(d, h, mlp) for _ in range(cfg["depth"])])
-        self.single_blocks = torch.nn.ModuleList([_SingleBlock(d, h, mlp) for _ in range(cfg["depth_single"])])
-        self.final_norm = torch.nn.LayerNorm(d, elementwise_affine=False, eps=1e-6)
-        self.final_adaln = torch.nn.Linear(d, 2 * d)
-        self.final_linear = torch.nn.Linear(d, cfg["in_channels"])
-
-    def pe(self, ids):
-        return torch.cat([_rope(ids[..., i], a, self.cfg["theta"]) for i, a in enumerate(self.cfg["axes"])],
-                         dim=-3).unsqueeze(1)
-
-    def forward(self, img, txt, pe, t, y, guidance):
-        img = self.img_in(img)
-        vec = self.time_in(_timestep_embedding(t).to(img.dtype))
-        vec = vec + self.guidance_in(_timestep_embedding(guidance).to(img.dtype))
-        vec = vec + self.vector_in(y)
-        txt = self.txt_in(txt)
-        for blk in self.double_blocks:
-            img, txt = blk(img, txt, vec, pe)
-        x = torch.cat([txt, img], dim=1)
-        for blk in self.single_blocks:
-            x = blk(x, vec, pe)
-        x = x[:, txt.shape[1]:]
-        shift, scale = self.final_adaln(torch.nn.functional.silu(vec)).chunk(2, dim=1)
-        x = torch.addcmul(shift[:, None], self.final_norm(x), 1 + scale[:, None])
-        return self.final_linear(x)
-
-
-def build_flux_dit(device, seed, cfg=FLUX_DEV):
-    """Random-init FLUX DiT in bf16: linears W ~ N(0, 0.02), bias ~ N(0, 0.01)."""
-
-    with torch.device(device):
-        model = FluxDiT(cfg)
-    g = torch.Generator(device=device).manual_seed(seed)
-    with torch.no_grad():
-        for m in model.modules():
-            if isinstance(m, torch.nn.Linear):
-                m.weight.normal_(0.0, 0.02, generator=g)
-                if m.bias is not None:
-                    m.bias.normal_(0.0, 0.01, generator=g)
-    return model.to(torch.bfloat16).eval()
-
-
-def dit_inputs(batch, device, seed, cfg=FLUX_DEV, img_tokens=1024, txt_tokens=512):
-    g = torch.Generator(device=device).manual_seed(seed)
-    side = int(round(img_tokens ** 0.5))
-    img = torch.randn((batch, img_tokens, cfg["in_channels"]), generator=g, device=device).to(torch.bfloat16)
-    txt = torch.randn((batch, txt_tokens, cfg["context"]), generator=g, device=device).to(torch.bfloat16)
-    y = torch.randn((batch, cfg["vec"]), generator=g, device=device).to(torch.bfloat16)
-    img_ids = torch.zeros((batch, img_tokens, 3), device=device)
-    img_ids[..., 1] = torch.arange(side, device=device)[:, None].expand(side, side).reshape(-1)
-    img_ids[..., 2] = torch.arange(side, device=device)[None, :].expand(side, side).reshape(-1)
-    ids = torch.cat([torch.zeros((batch, txt_tokens, 3), device=device), img_ids], dim=1)
-    return img, txt, y, ids
-
-
-def run_dit(args, rank, world, local):
-    """20 denoise steps of the FLUX DiT on 1024 image + 512
-    text tokens, batch 8 split data-parallel over the ranks (no collective),
-    dense bf16 and with every eligible linear swapped for ConvRotLinear
-    (mpp-w4a4, g256).  One denoise step (forward + Euler update) is captured
-    as a CUDA graph; the 20-step loop is timed with CUDA events, max over
-    ranks."""
-
+    import flux_dit
     from convrot_mlx_b200 import _lib
     from convrot_mlx_b200.adapter import replace_convrot_linears
 
@@ -801,17 +674,17 @@ def run_dit(args, rank, world, local):
     if total_batch % world:
         raise SystemExit(f"batch {total_batch} does not split over {world} GPUs")
     b = total_batch // world
-    model = build_flux_dit(device, SEED)
-    img, txt, y, ids = dit_inputs(b, device, SEED + 7 + rank)
+    model = flux_dit.build_flux_dit(device, SEED)
+    img, txt, y, ids = flux_dit.dit_inputs(b, device, SEED + 7 + rank)
     with torch.no_grad():
-        pe = model.pe(ids)
+        rope = model.rotary(ids)
     guidance = torch.full((b,), 3.5, device=device)
     ts = torch.linspace(1.0, 0.0, steps_per_gen + 1, device=device)
     t_cur, t_next = torch.zeros((b,), device=device), torch.zeros((b,), device=device)
     x = img.clone()
 
     def denoise_step():
-        v = model(x, txt, pe, t_cur, y, guidance)
+        v = model(x, txt, rope, t_cur, y, guidance)
         x.add_((t_next - t_cur)[:, None, None].to(x.dtype) * v)
 
     def generation_ms(reps):
@@ -832,7 +705,7 @@ def run_dit(args, rank, world, local):
                 graph.replay()
 
         with torch.cuda.stream(stream):
-            for _ in range(max(1, args.warmup)):
+            for _ in range(max(1, warm_gens)):
                 generation()
         torch.cuda.synchronize()
         barrier(world)
@@ -848,44 +721,46 @@ def run_dit(args, rank, world, local):
         del graph
         return ms
 
-    dense_ms = generation_ms(args.steps)
+    dense_ms = generation_ms(gens)
     replaced = replace_convrot_linears(model, backend="mpp-w4a4")
     torch.cuda.empty_cache()
+    fused = hasattr(replaced and dict(model.named_modules())[replaced[0]], "forward_modulated_norm")
+    model.fuse_modulated_norm = fused
     with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
-        w4_ms = generation_ms(args.steps)
-    d = FLUX_DEV["hidden"]
-    mlp = int(d * FLUX_DEV["mlp_ratio"])
-    per_sample = (FLUX_DEV["depth"] * 2 * (1024 + 512) * d * (3 * d + d + 2 * mlp)
-                  + FLUX_DEV["depth_single"] * 2 * 1536 * (d * (3 * d + mlp) + (d + mlp) * d))
-    linear_ops = per_sample * total_batch * steps_per_gen
+        w4_ms = generation_ms(gens)
+    linear_ops = flux_dit.linear_ops_per_sample() * total_batch * steps_per_gen
+    err = _lib.take_device_error()
+    del model
+    torch.cuda.empty_cache()
     return {
-        "metric": "FLUX DiT 20-step generation latency, batch 8 split over the GPUs (BASELINE config 4)",
-        "value": round(w4_ms, 2), "unit": "ms", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(w4_ms / steps_per_gen, 3), "higher_is_better": False, "scaling": "strong",
-        "vs_baseline": None, "dtype": "W4A4 int8 tensor (eligible linears), bf16 elsewhere",
-        "data": "synthetic, seeded: random-init FLUX.1-dev architecture, W ~ N(0, 0.02), latents/text/vector ~ N(0, 1)",
-        "config": {"workload": "flux-dit (BASELINE config 4)", "batch": total_batch, "per_gpu_batch": b,
-                   "tokens": "1024 image + 512 text", "denoise_steps": steps_per_gen,
-                   "parallelism": f"dp{world} (batch split, no collective)", "linears_w4a4": len(replaced),
-                   "timing": "one denoise step as a CUDA graph, 20 replays per generation, CUDA events, max over ranks"},
-        "dense_bf16_ms": round(dense_ms, 2), "speedup_vs_dense_bf16": round(dense_ms / w4_ms, 3),
-        "linear_tops": round(linear_ops / (w4_ms * 1e-3) / 1e12, 1),
-        "clocks": dict(clocks.summary(), window="nvidia-smi samples during the timed W4A4 generations"),
-        "device_error": _lib.take_device_error(),
+        "w4a4_ms": round(w4_ms, 2), "dense_bf16_ms": round(dense_ms, 2),
+        "speedup_vs_dense_bf16": round(dense_ms / w4_ms, 3),
+        "w4a4_ms_per_denoise_step": round(w4_ms / steps_per_gen, 3), "n_gpus": world, "per_gpu_batch": b,
+        "batch": total_batch, "denoise_steps": steps_per_gen, "generations_timed": gens,
+        "linears_w4a4": len(replaced), "linear_tops": round(linear_ops / (w4_ms * 1e-3) / 1e12, 1),
+        "fused_modulated_norm": fused, "parallelism": f"dp{world} (batch split, no collective)",
+        "clocks": clocks.summary(), "device_error": err,
     }
 
+
+# ---------------------------------------------------------------------------
+# video-DiT linears, tensor parallel over the ranks
 
 VIDEO_M = 32760
 VIDEO_KN = ((5120, 15360), (5120, 13824), (13824, 5120))
 
 
-def run_video_tp(args, rank, world, local):
-    """large video-DiT linears, weights N-split over the
-    ranks (ColumnParallelConvRotLinear), the all-gather of the outputs fused
-    into the GEMM epilogue (peer stores) plus a flag barrier.  One step = the
-    three linears on M = 32760 tokens.  Timed eagerly (the barrier epoch
-    advances every call) with CUDA events, max over ranks; also timed with
-    each rank's GEMMs writing only its own shard (no exchange) for the split."""
+def run_video_tp(args, rank, world, local, steps: int, warmup: int):
+    """Large video-DiT linears with the weights N-split over the ranks
+    (``ColumnParallelConvRotLinear``): the all-gather of the outputs is fused
+    into the GEMM epilogue (peer stores), then a flag barrier.  One step = the
+    three linears on M = 32760 tokens, timed eagerly (the barrier epoch
+    advances every call) with CUDA events, max over ranks.  Also timed: each
+    rank's GEMMs writing only its own shard (compute only), and the same
+    shard GEMMs followed by an NCCL all_gather_into_tensor and the permute to
+    (M, N) (the library-collective arm).  Parity: every rank compares the
+    gathered output of each linear with the single-GPU ConvRotLinear of the
+    full weight, bit for bit."""
 
     import ctypes
 
@@ -894,7 +769,7 @@ def run_video_tp(args, rank, world, local):
     from convrot_mlx_b200.tp import ColumnParallelConvRotLinear
 
     device = torch.device("cuda", local if world > 1 else 0)
-    if world == 1 and not torch.distributed.is_initialized():
+    if not torch.distributed.is_initialized():
         # the layer keeps its output in symmetric memory, which needs a process group
         import datetime
         import socket
@@ -904,69 +779,99 @@ def run_video_tp(args, rank, world, local):
             port = sock.getsockname()[1]
         torch.distributed.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
                                              timeout=datetime.timedelta(seconds=120), device_id=device)
-    layers, xs = [], []
+    layers, fulls, xs = [], [], []
     for i, (k, n) in enumerate(VIDEO_KN):
         full, _, _ = make_linear(k, n, SEED + 50 + i, device)
         layers.append(ColumnParallelConvRotLinear.from_full(full))
-        del full
+        fulls.append(full)
         xs.append(make_activation(VIDEO_M, k, SEED + 60 + i, device))
     torch.cuda.synchronize()
     lib = _lib.load()
+
+    # parity first: the gathered output of every linear against the full layer
+    parity = True
+    for layer, full, x in zip(layers, fulls, xs):
+        got = layer(x)
+        want = full(x)
+        torch.cuda.synchronize()
+        parity &= bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+        del want
+    if world > 1:
+        flag = torch.tensor([0 if parity else 1], dtype=torch.int32, device=device)
+        torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MAX)
+        parity = int(flag.item()) == 0
+    del fulls
+    torch.cuda.empty_cache()
 
     def step():
         for layer, x in zip(layers, xs):
             layer(x)
 
-    def local_only():
-        # the same GEMMs writing only this rank's shard into its own buffer
-        for layer, x in zip(layers, xs):
-            out, _, _ = layer._output(VIDEO_M, x.dtype, 0)
-            codes, xsc = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
-            one = (ctypes.c_void_p * 1)(out.data_ptr())
-            _lib.check(lib.convrot_w4a4_gemm_gather(_lib.ptr(codes), _lib.ptr(layer.qweight), layer.layout,
-                                                    _lib.ptr(xsc), _lib.ptr(layer.scales), _lib.ptr(layer.bias), one, 1,
-                                                    layer.out_features, layer.start, _lib.BF16, VIDEO_M,
-                                                    layer.shard_features, layer.in_features, _lib.stream_of(x)), "gemm")
+    shards = [torch.empty((VIDEO_M, layer.shard_features), dtype=torch.bfloat16, device=device) for layer in layers]
 
-    def timed(fn, steps):
-        for _ in range(args.warmup):
+    def shard_gemms(i):
+        layer, x = layers[i], xs[i]
+        codes, xsc = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
+        one = (ctypes.c_void_p * 1)(shards[i].data_ptr())
+        _lib.check(lib.convrot_w4a4_gemm_gather(_lib.ptr(codes), _lib.ptr(layer.qweight), layer.layout,
+                                                _lib.ptr(xsc), _lib.ptr(layer.scales), _lib.ptr(layer.bias), one, 1,
+                                                layer.shard_features, 0, _lib.BF16, VIDEO_M, layer.shard_features,
+                                                layer.in_features, _lib.stream_of(x)), "gemm")
+
+    def local_only():
+        for i in range(len(layers)):
+            shard_gemms(i)
+
+    gathered = [torch.empty((world * VIDEO_M, layer.shard_features), dtype=torch.bfloat16, device=device)
+                for layer in layers] if world > 1 else []
+    full_out = [torch.empty((VIDEO_M, layer.out_features), dtype=torch.bfloat16, device=device)
+                for layer in layers] if world > 1 else []
+
+    def nccl_step():
+        for i, layer in enumerate(layers):
+            shard_gemms(i)
+            torch.distributed.all_gather_into_tensor(gathered[i], shards[i])
+            full_out[i].view(VIDEO_M, world, layer.shard_features).copy_(
+                gathered[i].view(world, VIDEO_M, layer.shard_features).transpose(0, 1))
+
+    def timed(fn, n):
+        for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(steps):
+        for _ in range(n):
             fn()
         e1.record()
         torch.cuda.synchronize()
         barrier(world)
-        return max_over_ranks(e0.elapsed_time(e1), world)
+        return max_over_ranks(e0.elapsed_time(e1), world) / n
 
     with ClockSampler(str(torch.cuda.get_device_properties(device).uuid)) as clocks:
-        elapsed_ms = timed(step, args.steps)
-    local_ms = timed(local_only, args.steps) / args.steps
+        ms = timed(step, steps)
+    local_ms = timed(local_only, steps)
+    nccl_ms = timed(nccl_step, steps) if world > 1 else None
     ops = sum(2 * VIDEO_M * k * n for k, n in VIDEO_KN)
-    ms_per_step = elapsed_ms / args.steps
-    err = _lib.take_device_error()
+    out_bytes = sum(VIDEO_M * n * 2 for k, n in VIDEO_KN)
+    recv = out_bytes * (world - 1) // world
+    exch = ms - local_ms
     line = {
-        "metric": "video-DiT linears W4A4 tensor-parallel TOPS (BASELINE config 5)",
-        "value": round(ops / (ms_per_step * 1e-3) / 1e12, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "int8 (A4 codes x W4 nibbles, int32 accumulate), bf16 I/O",
-        "data": "synthetic, seeded: W ~ N(0, 0.02), bias ~ N(0, 0.01), x ~ N(0, 1) with 1% outlier channels x20",
-        "config": {"workload": "video-tp (BASELINE config 5)", "m": VIDEO_M, "kn": [list(p) for p in VIDEO_KN],
-                   "group_size": GROUP, "parallelism": f"tp{world} (N split, all-gather fused into the GEMM epilogue)",
-                   "timing": "eager launches between CUDA events, max over ranks"},
-        "compute_only_ms_per_step": round(local_ms, 4),
-        "exchange_overhead_ms_per_step": round(ms_per_step - local_ms, 4),
-        "gathered_bytes_per_rank_per_step": sum(VIDEO_M * n * 2 * (world - 1) // world for k, n in VIDEO_KN),
-        "gpu_launches": 3 * 3 * args.steps,
-        "clocks": dict(clocks.summary(), window="nvidia-smi samples during the timed steps"),
-        "device_error": err,
+        "tops": round(ops / (ms * 1e-3) / 1e12, 2), "ms_per_step": round(ms, 4), "n_gpus": world,
+        "parity_bit_exact": parity, "compute_only_ms": round(local_ms, 4), "exchange_ms": round(exch, 4),
+        "received_bytes_per_rank": recv,
+        "exchange_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1) if world > 1 else None,
+        "nccl_allgather_arm_ms": None if nccl_ms is None else round(nccl_ms, 4),
+        "nccl_allgather_arm_tops": None if nccl_ms is None else round(ops / (nccl_ms * 1e-3) / 1e12, 2),
+        "m": VIDEO_M, "kn": [list(p) for p in VIDEO_KN],
+        "parallelism": f"tp{world} (N split; all-gather fused into the GEMM epilogue as peer stores)",
+        "clocks": clocks.summary(), "device_error": _lib.take_device_error(),
     }
     for layer in layers:
         layer._out.clear()
         layer._flags = None
+    del layers, xs, shards, gathered, full_out
+    torch.cuda.empty_cache()
     return line
 
 
@@ -999,6 +904,29 @@ def run_case(args):
     return 1 if err else 0
 
 
+def summarize(line):
+    """Headline figures at the end of the JSON line (where a tail keeps them)."""
+
+    s = {"value_tops": line["value"], "speedup_vs_dense_bf16": line["speedup_vs_dense_bf16"],
+         "dense_bf16_tflops": line["dense_bf16"]["value"], "gemm_frac": line["roofline"]["frac"],
+         "gemm_frac_of_2x_bf16": line["roofline"]["frac_of_2x_measured_bf16"],
+         "prep_frac": line["roofline_prep"]["frac"], "w4a16_speedup_vs_dense": line["w4a16"]["speedup_vs_dense_bf16"],
+         "e2e_tops": line["e2e"]["value"]}
+    c2 = line.get("c2_prep")
+    if c2:
+        s["c2_prep_frac"] = {"g64": c2["g64"]["frac"], "g256": c2["g256"]["frac"]}
+    tp = line.get("video_tp")
+    if tp:
+        s["video_tp"] = {"n_gpus": tp["n_gpus"], "tops": tp["tops"], "ms": tp["ms_per_step"],
+                         "parity": tp["parity_bit_exact"], "compute_ms": tp["compute_only_ms"],
+                         "exchange_ms": tp["exchange_ms"], "nccl_arm_ms": tp["nccl_allgather_arm_ms"]}
+    dit = line.get("dit")
+    if dit:
+        s["dit"] = {"n_gpus": dit["n_gpus"], "w4a4_ms": dit["w4a4_ms"], "dense_ms": dit["dense_bf16_ms"],
+                    "speedup": dit["speedup_vs_dense_bf16"]}
+    return s
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1006,9 +934,11 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", choices=("flux-sweep", "video-tp", "dit"), default="flux-sweep",
-                    help="flux-sweep: BASELINE config 3 (default); video-tp: config 5, tensor-parallel over --gpus; "
-                         "dit: config 4, FLUX DiT with the batch split over --gpus")
+    ap.add_argument("--workload", choices=("all", "flux-sweep", "video-tp", "dit"), default="all",
+                    help="all (default): the config-3 FLUX sweep line with the config-2 prep, config-5 "
+                         "tensor-parallel and config-4 DiT entries added; flux-sweep: config 3 alone; video-tp: "
+                         "config 5 alone; dit: config 4 alone")
+    ap.add_argument("--dit-gens", type=int, default=2, help="timed 20-step generations per DiT arm in --workload all")
     ap.add_argument("--case", choices=("gemm", "prep"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=3072)
@@ -1028,19 +958,29 @@ def main(argv=None):
             print(json.dumps(line), flush=True)
         return 0
     rank, world, local = dist_setup(args.gpus)
+    rc = 0
     try:
+        device = torch.device("cuda", local if world > 1 else 0)
         if args.workload == "video-tp":
-            line = run_video_tp(args, rank, world, local)
+            line = run_video_tp(args, rank, world, local, args.steps, args.warmup)
+            rc = 0 if line["parity_bit_exact"] else 1
         elif args.workload == "dit":
-            line = run_dit(args, rank, world, local)
+            line = run_dit(args, rank, world, local, args.steps, args.warmup)
         else:
             line = run_ours(args, rank, world, local)
+            if args.workload == "all":
+                torch.cuda.empty_cache()
+                line["c2_prep"] = run_c2(args, device)
+                line["video_tp"] = run_video_tp(args, rank, world, local, min(args.steps, 10), min(args.warmup, 2))
+                line["dit"] = run_dit(args, rank, world, local, args.dit_gens, 1)
+                rc = 0 if line["video_tp"]["parity_bit_exact"] else 1
+            line["summary"] = summarize(line)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
         if torch.distributed.is_initialized():
             torch.distributed.destroy_process_group()
-    return 0
+    return rc
 
 
 if __name__ == "__main__":

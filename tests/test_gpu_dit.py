@@ -1,4 +1,4 @@
-"""The FLUX-architecture DiT of bench.py with its eligible
+"""The FLUX-architecture DiT of flux_dit.py with its eligible
 linears swapped by replace_convrot_linears: every swapped layer equals a
 ConvRotLinear built by hand from the same dense weight (bit for bit), and
 the W4A4 model stays close to the dense bf16 one (a loose sanity bound: W4A4
@@ -9,18 +9,18 @@ from __future__ import annotations
 import pytest
 import torch
 
-import bench
+import flux_dit
 import convrot_mlx_b200 as cr
 from convrot_mlx_b200.adapter import replace_convrot_linears
 from tests.gpu_util import assert_no_device_error, dev
 
 pytestmark = pytest.mark.gpu
 
-TINY = dict(bench.FLUX_DEV, hidden=512, heads=4, depth=2, depth_single=2, context=512, vec=256)
+TINY = dict(flux_dit.FLUX_DEV, hidden=512, heads=4, depth=2, depth_single=2, context=512, vec=256)
 
 
 def test_swapped_layers_match_hand_built_layers():
-    model = bench.build_flux_dit(dev(), 5, TINY)
+    model = flux_dit.build_flux_dit(dev(), 5, TINY)
     dense = {n: m.weight.detach().clone() for n, m in model.named_modules() if isinstance(m, torch.nn.Linear)}
     biases = {n: m.bias.detach().clone() for n, m in model.named_modules() if isinstance(m, torch.nn.Linear)}
     names = replace_convrot_linears(model, backend="mpp-w4a4")
@@ -38,12 +38,12 @@ def test_swapped_layers_match_hand_built_layers():
 
 
 def test_w4a4_dit_tracks_dense_dit():
-    model = bench.build_flux_dit(dev(), 6, TINY)
-    img, txt, y, ids = bench.dit_inputs(2, dev(), 7, TINY, img_tokens=64, txt_tokens=32)
+    model = flux_dit.build_flux_dit(dev(), 6, TINY)
+    img, txt, y, ids = flux_dit.dit_inputs(2, dev(), 7, TINY, img_tokens=64, txt_tokens=32)
     t = torch.tensor([0.7, 0.3], device=dev())
     guide = torch.full((2,), 3.5, device=dev())
     with torch.no_grad():
-        pe = model.pe(ids)
+        pe = model.rotary(ids)
         want = model(img, txt, pe, t, y, guide).float()
         replace_convrot_linears(model, backend="mpp-w4a4")
         got = model(img, txt, pe, t, y, guide).float()

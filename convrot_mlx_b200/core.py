@@ -272,6 +272,54 @@ def quantize_convrot_weight(
     return _prepare(weight, group_size, packed=True)
 
 
+def _mod_vectors(v: torch.Tensor, batch: int, features: int) -> tuple[torch.Tensor, int]:
+    """A (batch, [1,] features) modulation vector as (tensor, sample stride)
+    that the fused kernel can read: unit stride along features, 16-byte
+    aligned, sample stride a multiple of 8 elements (else a packed copy)."""
+
+    v2 = v.reshape(v.shape[0], v.shape[-1]) if v.ndim == 3 else v
+    if v2.ndim != 2 or v2.shape[-1] != features or v2.shape[0] not in (1, batch):
+        raise ValueError(f"modulation vector of shape {tuple(v.shape)} does not match ({batch}, 1, {features})")
+    if v2.shape[0] == 1 and batch > 1:
+        v2 = v2.expand(batch, features)
+    stride = v2.stride(0)
+    if v2.stride(1) != 1 or stride % 8 or v2.data_ptr() % 16 or v2.dtype != torch.bfloat16:
+        v2 = v2.to(torch.bfloat16).contiguous()
+        stride = features
+    return v2, stride
+
+
+def modulated_norm_prepare_i8(x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, eps: float = 1e-6,
+                              group_size: int = CONVROT_GROUP_SIZE) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 codes and row scales of ``prepare(addcmul(shift, layer_norm(x), 1 + scale))``
+    in one kernel (``convrot_modnorm_prepare_i8``).  x: (batch, tokens,
+    features) or (rows, features) bf16 (then one modulation row); returns
+    codes (rows, features) int8 and scales (rows,) float32."""
+
+    _require_cuda(x, shift, scale)
+    if x.dtype != torch.bfloat16:
+        raise ValueError(f"the fused modulated-norm prep takes bfloat16 activations, got {x.dtype}")
+    features = x.shape[-1]
+    x3 = x.reshape(1, -1, features) if x.ndim == 2 else x.reshape(x.shape[0], -1, features)
+    batch, tokens = x3.shape[0], x3.shape[1]
+    x2 = x3.reshape(-1, features).contiguous()
+    sh, sh_stride = _mod_vectors(shift, batch, features)
+    sc, sc_stride = _mod_vectors(scale, batch, features)
+    if sh_stride != sc_stride:
+        sh, sc = sh.contiguous(), sc.contiguous()
+        sh_stride = sc_stride = features
+    rows = x2.shape[0]
+    codes = torch.empty((rows, features), dtype=torch.int8, device=x.device)
+    scales = torch.empty((rows,), dtype=torch.float32, device=x.device)
+    _lib.check(
+        _lib.load().convrot_modnorm_prepare_i8(
+            _lib.ptr(x2), _lib.BF16, rows, features, group_size, _lib.ptr(sh), _lib.ptr(sc), max(tokens, 1),
+            sh_stride, float(eps), _lib.ptr(codes), _lib.ptr(scales), _lib.stream_of(x2)),
+        "modulated-norm activation preparation",
+    )
+    return codes, scales
+
+
 # ---------------------------------------------------------------------------
 # GEMMs
 
@@ -541,6 +589,30 @@ class ConvRotLinear(nn.Module):
                               m, self.out_features, self.in_features)
             return out.reshape(*lead, self.out_features)
         codes, xscales = _prepare(x2d, self.group_size, packed=False)
+        out = _gemm_w4a4(codes, self.qweight, self.layout_code, xscales, self.scales, self.bias, x.dtype,
+                         m, self.out_features, self.in_features)
+        return out.reshape(*lead, self.out_features)
+
+    def forward_modulated_norm(self, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                               eps: float = 1e-6) -> torch.Tensor:
+        """``self(torch.addcmul(shift, layer_norm(x), 1 + scale))`` with the norm,
+        the modulation, the rotation and the A4 quantization in one kernel
+        (``modulated_norm_prepare_i8``), then the W4A4 GEMM.
+
+        An extension for DiT blocks (no counterpart in the reference, whose
+        design notes name the activation-preparation passes as the remaining
+        cost, docs/design.md:54-64).  x: (batch, tokens, in_features) bf16;
+        shift / scale: (batch, 1, in_features) or (batch, in_features).  The
+        W4A16 backend takes the unfused path (it quantizes no activation)."""
+
+        if x.shape[-1] != self.in_features:
+            raise ValueError(f"ConvRotLinear expected K={self.in_features}, got {x.shape[-1]}")
+        if self.backend == "mpp-w4a16" or x.dtype != torch.bfloat16 or self.group_size not in (64, 256):
+            normed = torch.nn.functional.layer_norm(x, (x.shape[-1],), eps=eps)
+            return self(torch.addcmul(shift, normed, 1 + scale))
+        lead = x.shape[:-1]
+        codes, xscales = modulated_norm_prepare_i8(x, shift, scale, eps, self.group_size)
+        m = codes.shape[0]
         out = _gemm_w4a4(codes, self.qweight, self.layout_code, xscales, self.scales, self.bias, x.dtype,
                          m, self.out_features, self.in_features)
         return out.reshape(*lead, self.out_features)

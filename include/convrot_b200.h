@@ -85,6 +85,25 @@ int convrot_rotate(const void* x, int dtype, int64_t rows, int64_t features,
                    int group_size, void* out, void* stream);
 
 /*
+ * Modulated LayerNorm fused into the prep: the int8 codes and row scales of
+ * convrot_prepare_i8 applied to xm = bf16(fma(bf16(LayerNorm(x)),
+ * bf16(1 + scale), shift)), the input of a FLUX-style DiT projection, with x
+ * read once.  LayerNorm has no affine terms: mean and variance of the row in
+ * float32, y = bf16((x - mean) * rsqrt(var + eps)).  shift / scale: one
+ * bfloat16 vector of `features` per sample, sample s at s * mod_stride
+ * elements (mod_stride % 8 == 0); row r belongs to sample r / rows_per_mod.
+ * x bfloat16 only; group_size 64 or 256.  Bit for bit convrot_prepare_i8 of
+ * the same xm; against a separate layer_norm + addcmul only the float32 order
+ * of the row statistics differs, which can move a code by one.
+ * No reference counterpart: it fuses the activation-preparation pass into the
+ * producing op, the cost the reference names in docs/design.md:54-64 (its
+ * prep alone is core.py:456-484).
+ */
+int convrot_modnorm_prepare_i8(const void* x, int dtype, int64_t rows, int64_t features, int group_size,
+                               const void* shift, const void* scale, int64_t rows_per_mod, int64_t mod_stride,
+                               float eps, int8_t* q_i8, float* scales, void* stream);
+
+/*
  * Packed int4 -> int8.  Replaces metal_unpack_signed_int4 (core.py:1014-1027;
  * Metal kernel core.py:915-922) and unpack_signed_int4 (core.py:108-120).
  * packed: n_bytes bytes; out: 2 * n_bytes int8 values in [-8, 7].

@@ -51,3 +51,41 @@ def test_w4a4_dit_tracks_dense_dit():
     rel = float((got - want).norm() / want.norm())
     assert 0.0 < rel < 0.5, rel
     assert_no_device_error()
+
+
+def test_fused_modulated_norm_codes_inside_the_dit(monkeypatch):
+    # every modulated-norm projection of a W4A4 DiT forward, fused: on the same
+    # inputs its codes equal those of layer_norm + addcmul + prep up to the
+    # float32 order of the LayerNorm statistics (a code off by one, rarely).
+    # Whole-model outputs are not compared: a random-init W4A4 model amplifies
+    # a single flipped code by orders of magnitude.
+    from convrot_mlx_b200.core import _prepare, modulated_norm_prepare_i8
+
+    model = flux_dit.build_flux_dit(dev(), 8, TINY)
+    img, txt, y, ids = flux_dit.dit_inputs(2, dev(), 9, TINY, img_tokens=64, txt_tokens=32)
+    t = torch.tensor([0.6, 0.2], device=dev())
+    guide = torch.full((2,), 3.5, device=dev())
+    stats = []
+    orig = cr.ConvRotLinear.forward_modulated_norm
+
+    def checked(self, x, shift, scale, eps=1e-6):
+        k = x.shape[-1]
+        fc, fs = modulated_norm_prepare_i8(x, shift, scale, eps, self.group_size)
+        xm = torch.addcmul(shift, torch.nn.functional.layer_norm(x, (k,), eps=eps), 1 + scale)
+        uc, us = _prepare(xm.reshape(-1, k), self.group_size, packed=False)
+        d = (fc.int() - uc.int()).abs()
+        stats.append((int(d.max()), float((d != 0).float().mean()), float(((fs - us).abs() / us).max())))
+        return orig(self, x, shift, scale, eps)
+
+    monkeypatch.setattr(cr.ConvRotLinear, "forward_modulated_norm", checked)
+    with torch.no_grad():
+        pe = model.rotary(ids)
+        replace_convrot_linears(model, backend="mpp-w4a4")
+        model.fuse_modulated_norm = True
+        out = model(img, txt, pe, t, y, guide)
+    assert bool(torch.isfinite(out.float()).all())
+    assert len(stats) == 4 * TINY["depth"] + TINY["depth_single"]
+    assert all(s[0] <= 1 for s in stats), stats
+    assert max(s[1] for s in stats) <= 1e-3, stats
+    assert max(s[2] for s in stats) <= 2.0 ** -7, stats
+    assert_no_device_error()

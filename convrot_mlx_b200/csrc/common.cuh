@@ -50,6 +50,14 @@ int device_sm_count();
 // whose bounded wait timed out) on the current device.
 int* device_error_word();
 
+namespace w4a4 {
+// Argument checks of convrot_w4a4_gemm (gemm_w4a4.cu); need_act false skips
+// the activation and row-scale pointers (for callers that produce them).
+int check_gemm_args(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
+                    const float* wscales, const void* out, int out_dtype, int64_t m, int64_t n, int64_t k,
+                    bool need_act);
+}  // namespace w4a4
+
 // ---------------------------------------------------------------------------
 // element types
 

@@ -84,6 +84,8 @@ constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBB
 
 constexpr int kMaxOuts = 8;
 
+bool force_single_cta_kernel();
+
 struct Params {
   const uint8_t* qweight;
   const float* xscales;
@@ -1223,15 +1225,26 @@ static int launch(const CUtensorMap& map, const Params& p, cudaStream_t stream) 
   return check_launch("w4a4 gemm");
 }
 
+// Test hook, read once per process: CONVROT_GEMM_KERNEL=single routes every
+// shape to the one-CTA kernel (so tests can cover it on shapes the CTA-pair
+// kernel would take).
+bool force_single_cta_kernel() {
+  static const bool forced = [] {
+    const char* v = getenv("CONVROT_GEMM_KERNEL");
+    return v != nullptr && strcmp(v, "single") == 0;
+  }();
+  return forced;
+}
+
 }  // namespace w4a4
-}  // namespace convrot
 
-extern "C" {
-
-int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
-                      const float* wscales, const float* bias, void* out, int out_dtype, int64_t m, int64_t n,
-                      int64_t k, void* stream) {
-  using namespace convrot;
+// Argument checks of convrot_w4a4_gemm, also run by callers that enqueue
+// other work before the GEMM (the allocation-free linear), so that a call the
+// GEMM would reject enqueues nothing.  With need_act false the activation
+// pointer (not yet produced) is not checked.
+int w4a4::check_gemm_args(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
+                          const float* wscales, const void* out, int out_dtype, int64_t m, int64_t n, int64_t k,
+                          bool need_act) {
   CONVROT_REQUIRE(layout == CONVROT_LAYOUT_NK || layout == CONVROT_LAYOUT_KN, CONVROT_ERR_INVALID, "unknown layout %d",
                   layout);
   CONVROT_REQUIRE(valid_dtype(out_dtype), CONVROT_ERR_INVALID, "unknown output dtype %d", out_dtype);
@@ -1243,9 +1256,24 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
                   "K x packed-N weights require even N, got %lld", static_cast<long long>(n));
   CONVROT_REQUIRE(m < (1LL << 31) && n < (1LL << 31) && k < (1LL << 31), CONVROT_ERR_UNSUPPORTED, "shape too large");
   if (m == 0) return CONVROT_OK;
-  CONVROT_REQUIRE(act && qweight && xscales && wscales && out, CONVROT_ERR_INVALID, "null pointer");
-  CONVROT_REQUIRE(aligned_to(act, 16) && aligned_to(qweight, 16) && aligned_to(out, 16), CONVROT_ERR_INVALID,
-                  "activation, weight and output must be 16-byte aligned");
+  CONVROT_REQUIRE((act || !need_act) && qweight && (xscales || !need_act) && wscales && out, CONVROT_ERR_INVALID,
+                  "null pointer");
+  CONVROT_REQUIRE((!need_act || aligned_to(act, 16)) && aligned_to(qweight, 16) && aligned_to(out, 16),
+                  CONVROT_ERR_INVALID, "activation, weight and output must be 16-byte aligned");
+  return CONVROT_OK;
+}
+
+}  // namespace convrot
+
+extern "C" {
+
+int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales,
+                      const float* wscales, const float* bias, void* out, int out_dtype, int64_t m, int64_t n,
+                      int64_t k, void* stream) {
+  using namespace convrot;
+  const int args_rc = w4a4::check_gemm_args(act, qweight, layout, xscales, wscales, out, out_dtype, m, n, k,
+                                            /*need_act=*/true);
+  if (args_rc != CONVROT_OK || m == 0) return args_rc;
   w4a4::Params p;
   p.qweight = qweight;
   p.xscales = xscales;
@@ -1262,8 +1290,7 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
                   "too many output tiles");
   p.layout = layout;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const char* force = getenv("CONVROT_GEMM_KERNEL");  // "single" selects the one-CTA kernel (A/B testing)
-  const bool use_pair = w4a4::pair_supported(layout, n, k) && !(force && strcmp(force, "single") == 0);
+  const bool use_pair = w4a4::pair_supported(layout, n, k) && !w4a4::force_single_cta_kernel();
   if (use_pair) {
     if (layout == CONVROT_LAYOUT_NK) {
       switch (out_dtype) {

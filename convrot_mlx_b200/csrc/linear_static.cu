@@ -13,7 +13,9 @@
 // Host code cannot use that array's name as a device address (in host code
 // it names a host-side stand-in), so its device address is looked up once
 // per device with cudaGetSymbolAddress, with that device current, on the
-// first call made on the device.
+// first call made on the device.  That lookup may load the module on the
+// device, which a stream capture does not allow: a first call made while its
+// stream is capturing is refused with a message instead.
 #include <mutex>
 #include <vector>
 
@@ -30,9 +32,10 @@ static __device__ __align__(256) uint8_t g_linear_scratch[kStaticScratchBytes];
 std::mutex g_scratch_mu;
 std::vector<uint8_t*> g_scratch_addr;  // device address of g_linear_scratch, per device
 
-// Device address of the scratch array on the current device (nullptr and an
-// error message on failure).
-uint8_t* scratch_on_current_device() {
+// Device address of the scratch array on the current device (nullptr with
+// *status and an error message on failure).
+uint8_t* scratch_on_current_device(cudaStream_t stream, int* status) {
+  *status = CONVROT_ERR_CUDA;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) {
     set_error("no current CUDA device");
@@ -41,6 +44,13 @@ uint8_t* scratch_on_current_device() {
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (static_cast<int>(g_scratch_addr.size()) <= dev) g_scratch_addr.resize(dev + 1, nullptr);
   if (g_scratch_addr[dev] == nullptr) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+      set_error("convrot_w4a4_linear_static: the first call on device %d looks up the scratch array's address, "
+                "which cannot happen inside a stream capture; make one call outside capture first", dev);
+      *status = CONVROT_ERR_UNSUPPORTED;
+      return nullptr;
+    }
     void* p = nullptr;
     const cudaError_t rc = cudaGetSymbolAddress(&p, g_linear_scratch);
     if (rc != cudaSuccess || p == nullptr) {
@@ -72,9 +82,15 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size, const
                   "%lld; use convrot_prepare_i8 + convrot_w4a4_gemm with a caller-provided buffer",
                   static_cast<long long>(m), static_cast<long long>(k), static_cast<long long>(need),
                   static_cast<long long>(kStaticScratchBytes));
+  // every check the GEMM would make, before the prep kernel is enqueued: a
+  // rejected call enqueues nothing
+  const int args_rc = w4a4::check_gemm_args(nullptr, qweight, layout, nullptr, wscales, out, out_dtype, m, n, k,
+                                            /*need_act=*/false);
+  if (args_rc != CONVROT_OK) return args_rc;
   if (m == 0) return CONVROT_OK;
-  uint8_t* scratch = scratch_on_current_device();
-  if (scratch == nullptr) return CONVROT_ERR_CUDA;
+  int status = CONVROT_OK;
+  uint8_t* scratch = scratch_on_current_device(static_cast<cudaStream_t>(stream), &status);
+  if (scratch == nullptr) return status;
   int8_t* codes = reinterpret_cast<int8_t*>(scratch);
   float* xscales = reinterpret_cast<float*>(scratch + codes_bytes);
   // Prep writes every code and every scale that the GEMM then reads, so the

@@ -4,9 +4,13 @@
  *
  * Every entry point takes device pointers, element counts and a cudaStream_t
  * (passed as void*, NULL = legacy default stream), enqueues its kernels on
- * that stream and returns at once.  Nothing here allocates device memory: the
- * caller owns every buffer.  Return value: CONVROT_OK (0) or a negative
- * status; convrot_last_error() then gives a message (thread-local).
+ * that stream and returns at once.  No entry point allocates device memory:
+ * the caller owns every buffer.  The library itself holds two device arrays
+ * per device it is loaded on, for as long as the process lives: a 4-byte
+ * error word, and the fixed CONVROT_LINEAR_STATIC_SCRATCH_BYTES (64 MiB)
+ * intermediate of convrot_w4a4_linear_static.  Return value: CONVROT_OK (0)
+ * or a negative status; convrot_last_error() then gives a message
+ * (thread-local).
  *
  * Each function names the reference interface it replaces, as
  * path:line in Lumenbeing/convrot-mlx (src/convrot_mlx/core.py).
@@ -201,7 +205,10 @@ int convrot_peer_barrier(uint32_t* const* flag_arrays, int world, int rank, uint
  *     (m x k up to about 67 million), else CONVROT_ERR_UNSUPPORTED.  Every
  *     GPU that loads the library holds the array until the process exits.
  *   - The first call on a device looks up the array's device address on
- *     that device (make it before any stream capture on the device).
+ *     that device; made while `stream` is capturing, it is refused with
+ *     CONVROT_ERR_UNSUPPORTED (make one call outside capture first).
+ *   - Every argument check of convrot_w4a4_gemm runs before anything is
+ *     enqueued: a rejected call touches neither the GPU nor the array.
  *   - All calls share the one array: calls whose work overlaps on the GPU
  *     (different streams, or other host threads) race and must not overlap.
  *     Every call rewrites all of the array it reads, so nothing from an

@@ -78,3 +78,103 @@ def test_static_linear_rejects_shapes_beyond_its_array():
                                         None, _lib.ptr(x), _lib.BF16, m, 256, k, _lib.stream_of(x))
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"scratch" in lib.convrot_last_error()
+
+
+def test_static_linear_rejections_enqueue_nothing():
+    # m == 0 is a no-op; a call the GEMM would reject (bad output dtype, K not a
+    # multiple of 32, odd N for K x packed-N) is refused before the prep kernel
+    # is enqueued, so the output buffer keeps its contents
+    lib = _lib.load()
+    m, k, n = 64, 1024, 256
+    x, q, ws, bias = _inputs(m, k, n, _lib.LAYOUT_KN, 21)
+    out = torch.full((m, n), 7.0, dtype=torch.bfloat16, device=dev())
+    s = _lib.stream_of(x)
+
+    def call(mm, nn, kk, out_dtype=_lib.BF16, layout=_lib.LAYOUT_KN):
+        return lib.convrot_w4a4_linear_static(_lib.ptr(x), _lib.BF16, 256, _lib.ptr(q), layout, _lib.ptr(ws),
+                                              _lib.ptr(bias), _lib.ptr(out), out_dtype, mm, nn, kk, s)
+
+    assert call(0, n, k) == _lib.OK
+    assert call(m, n, k, out_dtype=7) == _lib.ERR_INVALID
+    assert call(m, n, 1000) == _lib.ERR_INVALID
+    assert call(m, n - 1, k) == _lib.ERR_INVALID
+    assert call(m, n, k, layout=5) == _lib.ERR_INVALID
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
+    assert_no_device_error()
+
+
+_CAPTURE_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from convrot_mlx_b200 import _lib
+lib = _lib.load()
+dev = torch.device("cuda", 0)
+m, k, n = 128, 512, 256
+x = torch.randn((m, k), device=dev).to(torch.bfloat16)
+q = torch.randint(0, 256, (k, n // 2), device=dev, dtype=torch.uint8)
+ws = torch.rand((n,), device=dev) * 0.01
+out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+ref = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+s = torch.cuda.Stream(device=dev)
+torch.cuda.synchronize()
+
+def call(o):
+    return lib.convrot_w4a4_linear_static(_lib.ptr(x), _lib.BF16, 256, _lib.ptr(q), _lib.LAYOUT_KN, _lib.ptr(ws),
+                                          None, _lib.ptr(o), _lib.BF16, m, n, k, _lib.stream_of(x))
+
+g = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g, stream=s):
+    first = call(out)                                  # first call on the device, inside capture
+msg = lib.convrot_last_error().decode()
+with torch.cuda.stream(s):
+    second = call(ref)                                 # outside capture: looks the address up
+g2 = torch.cuda.CUDAGraph()
+with torch.cuda.graph(g2, stream=s):
+    third = call(out)                                  # address known: captured like any launch
+g2.replay()
+torch.cuda.synchronize()
+same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
+print(first, second, third, same, "capture" in msg)
+"""
+
+
+def test_static_linear_first_call_inside_capture_is_refused():
+    import subprocess
+    import sys
+
+    from tests.conftest import ROOT
+
+    res = subprocess.run([sys.executable, "-c", _CAPTURE_SCRIPT, str(ROOT)], capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 0, res.stderr[-2000:]
+    first, second, third, same, msg_ok = res.stdout.split()[-5:]
+    assert int(first) == _lib.ERR_UNSUPPORTED and msg_ok == "True"
+    assert int(second) == _lib.OK and int(third) == _lib.OK and same == "True"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs a second GPU")
+def test_static_linear_on_a_second_device():
+    # the array's address is looked up per device: a call with device 1 current
+    with torch.cuda.device(1):
+        d1 = torch.device("cuda", 1)
+        m, k, n = 512, 1024, 384
+        g = torch.Generator(device=d1).manual_seed(4)
+        x = torch.randn((m, k), generator=g, device=d1).to(torch.bfloat16)
+        w = torch.randint(-7, 8, (k, n), generator=g, device=d1, dtype=torch.int8)
+        import convrot_mlx_b200 as cr
+        q = cr.pack_signed_int4(w)
+        ws = torch.rand((n,), generator=g, device=d1) * 0.01
+        lib = _lib.load()
+        s = _lib.stream_of(x)
+        codes = torch.empty((m, k), dtype=torch.int8, device=d1)
+        xs = torch.empty((m,), dtype=torch.float32, device=d1)
+        want = torch.empty((m, n), dtype=torch.bfloat16, device=d1)
+        got = torch.empty((m, n), dtype=torch.bfloat16, device=d1)
+        _lib.check(lib.convrot_prepare_i8(_lib.ptr(x), _lib.BF16, m, k, 256, _lib.ptr(codes), _lib.ptr(xs), s), "p")
+        _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(codes), _lib.ptr(q), _lib.LAYOUT_KN, _lib.ptr(xs), _lib.ptr(ws), None,
+                                         _lib.ptr(want), _lib.BF16, m, n, k, s), "g")
+        _lib.check(lib.convrot_w4a4_linear_static(_lib.ptr(x), _lib.BF16, 256, _lib.ptr(q), _lib.LAYOUT_KN,
+                                                  _lib.ptr(ws), None, _lib.ptr(got), _lib.BF16, m, n, k, s), "static")
+        torch.cuda.synchronize(d1)
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))

@@ -653,6 +653,74 @@ def run_c2(args, device):
 
 
 # ---------------------------------------------------------------------------
+# few activation rows: the swap-AB GEMM (BASELINE config 1 and the FLUX
+# modulation linears at m = batch)
+
+SMALL_M_SHAPES = ((8, 3072, 18432), (8, 3072, 9216), (1, 3072, 18432), (64, 1024, 1024))
+
+
+def run_small_m(args, device):
+    """The W4A4 GEMM at m <= 64, HBM-bound on the packed weights: per shape,
+    a CUDA graph of launches over distinct weights (> L2 in total) replayed
+    between CUDA events; achieved GB/s = (packed weights + activation codes
+    + output) / time against MEASURED_PEAKS.json hbm_gbs.  Beside it the same
+    GEMM forced onto the CTA-pair kernel, and dense bf16 (cuBLAS) on the
+    same shape."""
+
+    from convrot_mlx_b200 import _lib
+
+    lib = _lib.load()
+    peaks = load_peaks()
+    stream = torch.cuda.Stream(device=device)
+    out = []
+    for (m, k, n) in SMALL_M_SHAPES:
+        w_bytes = k * n // 2
+        n_w = max(2, int(300e6 // w_bytes) + 1)
+        g = torch.Generator(device=device).manual_seed(m + k + n)
+        qs = [torch.randint(0, 256, (k, n // 2), generator=g, device=device, dtype=torch.uint8) for _ in range(n_w)]
+        codes = torch.randint(-7, 8, (m, k), generator=g, device=device, dtype=torch.int8)
+        xs = torch.rand((m,), generator=g, device=device)
+        ws = torch.rand((n,), generator=g, device=device) * 0.01
+        bias = torch.randn((n,), generator=g, device=device) * 0.01
+        o = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+
+        def launches():
+            st = _lib.stream_of(codes)
+            for q in qs:
+                _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(codes), _lib.ptr(q), _lib.LAYOUT_KN, _lib.ptr(xs), _lib.ptr(ws),
+                                                 _lib.ptr(bias), _lib.ptr(o), _lib.BF16, m, n, k, st), "gemm")
+
+        us = graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3
+        _lib.check(lib.convrot_set_gemm_route(2), "route")
+        pair_us = graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3
+        _lib.check(lib.convrot_set_gemm_route(3), "route")
+        swap_us = graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3
+        _lib.check(lib.convrot_set_gemm_route(0), "route")
+        dw = [torch.randn((n, k), generator=g, device=device).to(torch.bfloat16) for _ in range(max(2, n_w // 4))]
+        xd = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+        bd = bias.to(torch.bfloat16)
+        od = torch.empty((m, n), dtype=torch.bfloat16, device=device)
+
+        def dense():
+            for wd in dw:
+                torch.addmm(bd, xd, wd.t(), out=od)
+
+        dense_us = graph_ms(dense, max(3, args.steps), stream) / len(dw) * 1e3
+        algo = w_bytes + m * k + 2 * m * n + 8 * n + 4 * m
+        gbs = algo / (us * 1e-6) / 1e9
+        out.append({"m": m, "k": k, "n": n, "us": round(us, 2), "gbs": round(gbs, 1),
+                    "frac": round(gbs / peaks["hbm_gbs"], 4), "kernel": "swap-AB" if m <= 8 else "pair",
+                    "swap_ab_kernel_us": round(swap_us, 2), "pair_kernel_us": round(pair_us, 2),
+                    "dense_bf16_us": round(dense_us, 2), "speedup_vs_dense_bf16": round(dense_us / us, 2)})
+        del qs, dw
+    return {"kernel": "default routing: small_m_kernel (swap-AB tcgen05 kind::i8, K split over a cluster, DSMEM "
+                      "reduction) for m <= 8, else pair_gemm_kernel",
+            "bound": "hbm", "peak_gbs": peaks["hbm_gbs"],
+            "bytes_note": "packed weights K N / 2 + codes M K + bf16 output 2 M N + scales/bias 8 N + 4 M per launch",
+            "shapes": out}
+
+
+# ---------------------------------------------------------------------------
 # BASELINE config 4: the FLUX DiT, batch 8 split data-parallel (no collective)
 
 
@@ -916,6 +984,9 @@ def summarize(line):
     c2 = line.get("c2_prep")
     if c2:
         s["c2_prep_frac"] = {"g64": c2["g64"]["frac"], "g256": c2["g256"]["frac"]}
+    sm = line.get("small_m")
+    if sm:
+        s["small_m"] = [[x["m"], x["k"], x["n"], x["us"], x["frac"], x["speedup_vs_dense_bf16"]] for x in sm["shapes"]]
     tp = line.get("video_tp")
     if tp:
         s["video_tp"] = {"n_gpus": tp["n_gpus"], "tops": tp["tops"], "ms": tp["ms_per_step"],
@@ -972,6 +1043,7 @@ def main(argv=None):
             if args.workload == "all":
                 torch.cuda.empty_cache()
                 line["c2_prep"] = run_c2(args, device)
+                line["small_m"] = run_small_m(args, device)
                 line["video_tp"] = run_video_tp(args, rank, world, local, min(args.steps, 10), min(args.warmup, 2))
                 line["dit"] = run_dit(args, rank, world, local, args.dit_gens, 1)
                 rc = 0 if line["video_tp"]["parity_bit_exact"] else 1

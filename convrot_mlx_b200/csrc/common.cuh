@@ -50,6 +50,13 @@ int device_sm_count();
 // whose bounded wait timed out) on the current device.
 int* device_error_word();
 
+// Swap-AB W4A4 GEMM for few activation rows (gemm_small_m.cu): the shapes it
+// takes, and its launch after convrot_w4a4_gemm's argument checks.
+bool small_m_supported(int layout, int64_t m, int64_t n, int64_t k);
+int small_m_auto_rows();
+int launch_small_m(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales, const float* wscales,
+                   const float* bias, void* out, int out_dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream);
+
 namespace w4a4 {
 // Argument checks of convrot_w4a4_gemm (gemm_w4a4.cu); need_act false skips
 // the activation and row-scale pointers (for callers that produce them).

@@ -84,7 +84,7 @@ constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + STAGES * (kABytes + kBB
 
 constexpr int kMaxOuts = 8;
 
-bool force_single_cta_kernel();
+int forced_kernel();
 
 struct Params {
   const uint8_t* qweight;
@@ -1225,16 +1225,13 @@ static int launch(const CUtensorMap& map, const Params& p, cudaStream_t stream) 
   return check_launch("w4a4 gemm");
 }
 
-// Test hook, read once per process: CONVROT_GEMM_KERNEL=single routes every
-// shape to the one-CTA kernel (so tests can cover it on shapes the CTA-pair
-// kernel would take).
-bool force_single_cta_kernel() {
-  static const bool forced = [] {
-    const char* v = getenv("CONVROT_GEMM_KERNEL");
-    return v != nullptr && strcmp(v, "single") == 0;
-  }();
-  return forced;
-}
+// Kernel routing of convrot_w4a4_gemm: 0 automatic, 1 every shape to the
+// one-CTA kernel, 2 every shape the CTA-pair kernel takes to it, 3 every
+// shape the swap-AB kernel takes (m <= 64) to it (set by
+// convrot_set_gemm_route, for tests and A/B measurements).
+std::atomic<int> g_gemm_route{0};
+
+int forced_kernel() { return g_gemm_route.load(std::memory_order_relaxed); }
 
 }  // namespace w4a4
 
@@ -1290,7 +1287,10 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
                   "too many output tiles");
   p.layout = layout;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool use_pair = w4a4::pair_supported(layout, n, k) && !w4a4::force_single_cta_kernel();
+  const int forced = w4a4::forced_kernel();
+  if (((forced == 0 && m <= small_m_auto_rows()) || forced == 3) && small_m_supported(layout, m, n, k))
+    return launch_small_m(act, qweight, layout, xscales, wscales, bias, out, out_dtype, m, n, k, s);
+  const bool use_pair = w4a4::pair_supported(layout, n, k) && forced != 1;
   if (use_pair) {
     if (layout == CONVROT_LAYOUT_NK) {
       switch (out_dtype) {
@@ -1426,6 +1426,13 @@ int convrot_w4a16_gemm(const void* act, int act_dtype, const uint8_t* qweight, i
   if (act_dtype == CONVROT_BF16) { CONVROT_W4A16_OUT(CONVROT_LAYOUT_KN, KIND_BF16) }
   CONVROT_W4A16_OUT(CONVROT_LAYOUT_KN, KIND_F16)
 #undef CONVROT_W4A16_OUT
+}
+
+int convrot_set_gemm_route(int route) {
+  using namespace convrot;
+  CONVROT_REQUIRE(route >= 0 && route <= 3, CONVROT_ERR_INVALID, "GEMM route must be 0-3, got %d", route);
+  w4a4::g_gemm_route.store(route, std::memory_order_relaxed);
+  return CONVROT_OK;
 }
 
 // Read and clear the device-side error word set by a kernel whose bounded

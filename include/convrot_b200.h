@@ -223,6 +223,18 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
                                int64_t k, void* stream);
 
 /*
+ * Diagnostics: which kernel convrot_w4a4_gemm runs.  route 0 (the default):
+ * the swap-AB kernel for m <= 8 (k % 128 == 0; K x packed-N with n % 32 ==
+ * 0), else the CTA-pair kernel where it applies (k % 128 == 0; K x packed-N
+ * with n % 32 == 0), else the one-CTA kernel; route 1: the one-CTA kernel
+ * for every shape; route 2: the CTA-pair kernel wherever it applies (never
+ * the swap-AB one); route 3: the swap-AB kernel wherever it applies (m <=
+ * 64).  All give the same bits.  Process-wide; for tests and A/B timing.
+ * No reference counterpart.
+ */
+int convrot_set_gemm_route(int route);
+
+/*
  * Diagnostics: every wait inside the tcgen05 kernels is bounded; a kernel
  * whose wait times out stops early and records a non-zero code in a
  * device-side word.  This reads and clears that word (0 = no time-out).  It
@@ -232,7 +244,10 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
  * for A / packed weights, 13 accumulator buffer free, 14 A stage landed,
  * 15 expanded weights ready, 16 final MMA drain, 17 packed weights landed,
  * 18 expanded-weight slot free, 19 accumulator ready); 31 peer flag barrier;
- * 41 staged prep row copy.
+ * 41 staged prep row copy; 51-57 swap-AB small-m GEMM (51 packed-weight
+ * slot free, 52 activation stage landed, 53 expanded weights ready, 54
+ * packed weights landed, 55 expanded-weight slot free, 56 final MMA drain,
+ * 57 activation slot free).
  */
 int convrot_take_device_error(int* code);
 

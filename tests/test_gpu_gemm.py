@@ -19,15 +19,19 @@ from tests.gpu_util import assert_no_device_error, bf16_bits, cuda, host
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=["pair", "single"], autouse=True)
-def gemm_kernel(request, monkeypatch):
-    """Run every GEMM test on both tcgen05 kernels: the CTA-pair kernel (default
-    where it applies) and the one-CTA kernel (ragged K x packed-N weights)."""
-    if request.param == "single":
-        monkeypatch.setenv("CONVROT_GEMM_KERNEL", "single")
-    else:
-        monkeypatch.delenv("CONVROT_GEMM_KERNEL", raising=False)
-    return request.param
+@pytest.fixture(params=["auto", "single", "pair", "swap_ab"], autouse=True)
+def gemm_kernel(request):
+    """Run every GEMM test on each tcgen05 kernel: the default routing (the
+    swap-AB kernel for m <= 8, else the CTA-pair kernel where it applies),
+    the one-CTA kernel for every shape, the CTA-pair kernel for every shape
+    it takes, and the swap-AB kernel for every m <= 64 shape
+    (convrot_set_gemm_route)."""
+    from convrot_mlx_b200 import _lib
+
+    route = {"auto": 0, "single": 1, "pair": 2, "swap_ab": 3}[request.param]
+    _lib.check(_lib.load().convrot_set_gemm_route(route), "route")
+    yield request.param
+    _lib.check(_lib.load().convrot_set_gemm_route(0), "route")
 
 
 def test_edges_nk_and_kn_match_reference():

@@ -48,10 +48,10 @@ def timestep_features(t: torch.Tensor, width: int = 256, base: float = 10000.0, 
     return torch.cat((angles.cos(), angles.sin()), dim=1)
 
 
-def rotary_tables(ids: torch.Tensor, axes, theta: float):
-    """Cosine and sine tables, (batch, tokens, sum(axes) / 2) float32, for the
-    three-axis rotary embedding: the pairs of head dimensions of axis a turn
-    by ``position_a * theta ** (-2 j / width_a)``."""
+def rotary_tables(ids: torch.Tensor, axes, theta: float) -> torch.Tensor:
+    """Unit complex rotations, (batch, 1, tokens, sum(axes) / 2) complex64,
+    for the three-axis rotary embedding: the pairs of head dimensions of axis
+    a turn by ``position_a * theta ** (-2 j / width_a)``."""
 
     angles = []
     for a, width in enumerate(axes):
@@ -59,18 +59,16 @@ def rotary_tables(ids: torch.Tensor, axes, theta: float):
         inv_freq = theta ** (-2.0 * j / width)
         angles.append(ids[..., a].double()[..., None] * inv_freq)
     ang = torch.cat(angles, dim=-1)
-    return ang.cos().float(), ang.sin().float()
+    return torch.polar(torch.ones_like(ang), ang).to(torch.complex64)[:, None]
 
 
-def rotate_pairs(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+def rotate_pairs(x: torch.Tensor, rot: torch.Tensor) -> torch.Tensor:
     """Rotate consecutive pairs (x[2j], x[2j + 1]) of the head dimension of x
-    (batch, heads, tokens, dim) by the angles of ``rotary_tables``."""
+    (batch, heads, tokens, dim) by the angles of ``rotary_tables``: one
+    complex multiply per pair in float32, (x0 + i x1) (cos + i sin)."""
 
-    xf = x.float().unflatten(-1, (-1, 2))
-    even, odd = xf[..., 0], xf[..., 1]
-    c, s = cos[:, None], sin[:, None]
-    out = torch.stack((even * c - odd * s, even * s + odd * c), dim=-1)
-    return out.flatten(-2).to(x.dtype)
+    xc = torch.view_as_complex(x.float().unflatten(-1, (-1, 2)))
+    return torch.view_as_real(xc * rot).flatten(-2).to(x.dtype)
 
 
 class RMSNorm(nn.Module):
@@ -139,8 +137,8 @@ class Attention(nn.Module):
         return self.q_norm(q), self.k_norm(k), v
 
 
-def attend(q, k, v, cos, sin):
-    q, k = rotate_pairs(q, cos, sin), rotate_pairs(k, cos, sin)
+def attend(q, k, v, rot):
+    q, k = rotate_pairs(q, rot), rotate_pairs(k, rot)
     o = F.scaled_dot_product_attention(q, k, v)
     return o.transpose(1, 2).flatten(2)
 
@@ -160,11 +158,11 @@ class DoubleStreamBlock(nn.Module):
         h = modulated_linear(self.flags, mlp[0], x, mod[3], mod[4])
         return torch.addcmul(x, mod[5], mlp[2](mlp[1](h)))
 
-    def forward(self, img, txt, vec, cos, sin):
+    def forward(self, img, txt, vec, rot):
         im, tm = self.img_mod(vec), self.txt_mod(vec)
         tq, tk, tv = self.txt_attn.qkv_heads(modulated_linear(self.flags, self.txt_attn.qkv, txt, tm[0], tm[1]))
         iq, ik, iv = self.img_attn.qkv_heads(modulated_linear(self.flags, self.img_attn.qkv, img, im[0], im[1]))
-        a = attend(torch.cat((tq, iq), 2), torch.cat((tk, ik), 2), torch.cat((tv, iv), 2), cos, sin)
+        a = attend(torch.cat((tq, iq), 2), torch.cat((tk, ik), 2), torch.cat((tv, iv), 2), rot)
         n_txt = txt.shape[1]
         txt = torch.addcmul(txt, tm[2], self.txt_attn.proj(a[:, :n_txt]))
         img = torch.addcmul(img, im[2], self.img_attn.proj(a[:, n_txt:]))
@@ -185,12 +183,12 @@ class SingleStreamBlock(nn.Module):
         self.act = nn.GELU(approximate="tanh")
         self.modulation = Modulation(width, 3)
 
-    def forward(self, x, vec, cos, sin):
+    def forward(self, x, vec, rot):
         shift, scale, gate = self.modulation(vec)
         h = modulated_linear(self.flags, self.linear1, x, shift, scale)
         qkv, m = h.split((3 * self.width, self.mlp), dim=-1)
         q, k, v = split_heads(qkv, self.heads)
-        a = attend(self.q_norm(q), self.k_norm(k), v, cos, sin)
+        a = attend(self.q_norm(q), self.k_norm(k), v, rot)
         return torch.addcmul(x, gate, self.linear2(torch.cat((a, self.act(m)), dim=-1)))
 
 
@@ -227,17 +225,16 @@ class FluxDiT(nn.Module):
     def rotary(self, ids):
         return rotary_tables(ids, self.cfg["axes"], self.cfg["theta"])
 
-    def forward(self, img, txt, rope, t, y, guidance):
-        cos, sin = rope
+    def forward(self, img, txt, rot, t, y, guidance):
         dt = img.dtype
         vec = self.time_in(timestep_features(t).to(dt)) + self.guidance_in(timestep_features(guidance).to(dt))
         vec = vec + self.vector_in(y)
         img, txt = self.img_in(img), self.txt_in(txt)
         for blk in self.double_blocks:
-            img, txt = blk(img, txt, vec, cos, sin)
+            img, txt = blk(img, txt, vec, rot)
         x = torch.cat((txt, img), dim=1)
         for blk in self.single_blocks:
-            x = blk(x, vec, cos, sin)
+            x = blk(x, vec, rot)
         x = x[:, txt.shape[1]:]
         shift, scale = self.final_mod(vec)
         x = torch.addcmul(shift, F.layer_norm(x, (x.shape[-1],), eps=LN_EPS), 1 + scale)

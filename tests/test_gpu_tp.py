@@ -133,3 +133,33 @@ def test_column_parallel_layer_bit_exact(tmp_path):
     assert ctx.join(timeout=240) or ctx.join(timeout=60)
     for r in range(world):
         assert open(f"{path}.{r}").read() == "ok", f"rank {r}"
+
+
+def test_peer_barrier_times_out_cleanly():
+    # A world of two in which the other rank never arrives: rank 0's barrier
+    # kernel writes its own epoch and then polls a slot that nothing sets.
+    # Its wait is bounded (2 s): the kernel must give up, record device error
+    # 31, and leave the context usable for the next call.
+    import time
+
+    flags = [torch.zeros(2, dtype=torch.int32, device=dev()) for _ in range(2)]
+    ptrs = (ctypes.c_void_p * 2)(*[f.data_ptr() for f in flags])
+    lib = _lib.load()
+    t0 = time.perf_counter()
+    _lib.check(lib.convrot_peer_barrier(ctypes.cast(ptrs, ctypes.POINTER(ctypes.c_void_p)), 2, 0, 1,
+                                        _lib.stream_of(flags[0])), "barrier")
+    code = _lib.take_device_error()  # synchronizes
+    elapsed = time.perf_counter() - t0
+    assert code == 31
+    assert 1.5 < elapsed < 30.0, elapsed
+    # rank 0 wrote its epoch into slot 0 of both arrays; slot 1 stayed empty
+    assert flags[0].tolist() == [1, 0] and flags[1].tolist() == [1, 0]
+    # the GPU still answers: a world-of-one barrier and a small GEMM run normally
+    one = (ctypes.c_void_p * 1)(flags[1].data_ptr())
+    _lib.check(lib.convrot_peer_barrier(ctypes.cast(one, ctypes.POINTER(ctypes.c_void_p)), 1, 0, 5,
+                                        _lib.stream_of(flags[1])), "barrier")
+    layer = _layer(256, 64, 3, dev())
+    y = layer(torch.ones((4, 256), dtype=torch.bfloat16, device=dev()))
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(y.float()).all()) and int(flags[1][0].item()) == 5
+    assert_no_device_error()

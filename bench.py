@@ -743,6 +743,8 @@ def run_dit(args, rank, world, local, gens: int, warm_gens: int):
         raise SystemExit(f"batch {total_batch} does not split over {world} GPUs")
     b = total_batch // world
     model = flux_dit.build_flux_dit(device, SEED)
+    flux_dit.build_glue()
+    model.fuse_attention_glue = True  # both arms: the q/k norm + rotary + attention layout kernel
     img, txt, y, ids = flux_dit.dit_inputs(b, device, SEED + 7 + rank)
     with torch.no_grad():
         rope = model.rotary(ids)
@@ -807,7 +809,7 @@ def run_dit(args, rank, world, local, gens: int, warm_gens: int):
         "w4a4_ms_per_denoise_step": round(w4_ms / steps_per_gen, 3), "n_gpus": world, "per_gpu_batch": b,
         "batch": total_batch, "denoise_steps": steps_per_gen, "generations_timed": gens,
         "linears_w4a4": len(replaced), "linear_tops": round(linear_ops / (w4_ms * 1e-3) / 1e12, 1),
-        "fused_modulated_norm": True, "parallelism": f"dp{world} (batch split, no collective)",
+        "fused_modulated_norm": True, "attention_glue": "flux_dit_glue.cu (both arms)", "parallelism": f"dp{world} (batch split, no collective)",
         "clocks": clocks.summary(), "device_error": err,
     }
 

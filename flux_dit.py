@@ -26,11 +26,45 @@ rotation and the A4 quantization run as one kernel
 
 from __future__ import annotations
 
+import ctypes
 import math
+import shutil
+import subprocess
+from pathlib import Path
 
 import torch
 import torch.nn.functional as F
 from torch import nn
+
+_HERE = Path(__file__).resolve().parent
+_GLUE_SRC = _HERE / "flux_dit_glue.cu"
+_GLUE_LIB = _HERE / "libflux_dit_glue.so"
+_glue = None
+
+
+def build_glue(force: bool = False) -> Path:
+    """Compile ``flux_dit_glue.cu`` (the attention glue of this model: q/k
+    RMSNorm + rotary embedding + attention layout) for sm_100a, in-tree."""
+
+    if force or not _GLUE_LIB.exists() or _GLUE_LIB.stat().st_mtime < _GLUE_SRC.stat().st_mtime:
+        nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+        subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+                        "-Xcompiler", "-fPIC", "-shared", str(_GLUE_SRC), "-o", str(_GLUE_LIB)],
+                       check=True, capture_output=True)
+    return _GLUE_LIB
+
+
+def glue():
+    """The attention-glue library, or None when it was not built."""
+
+    global _glue
+    if _glue is None and _GLUE_LIB.exists():
+        lib = ctypes.CDLL(str(_GLUE_LIB))
+        P, I64 = ctypes.c_void_p, ctypes.c_int64
+        lib.flux_qk_norm_rope.argtypes = [P, I64, I64, I64, I64, P, P, ctypes.c_float, P, I64, I64, P, P, P, P]
+        lib.flux_qk_norm_rope.restype = ctypes.c_int
+        _glue = lib
+    return _glue
 
 FLUX_DEV = dict(hidden=3072, heads=24, mlp_ratio=4.0, depth=19, depth_single=38, in_channels=64, context=4096,
                 vec=768, axes=(16, 56, 56), theta=10000)
@@ -143,6 +177,38 @@ def attend(q, k, v, rot):
     return o.transpose(1, 2).flatten(2)
 
 
+def fused_attention_inputs(parts, rot, heads):
+    """q, k, v (batch, heads, tokens, 128) for attention from one or more
+    projection outputs, each (qkv rows (batch, tokens, >= 3 heads 128), its
+    Attention / block with q_norm and k_norm), placed side by side along the
+    tokens: the q/k RMSNorm, the rotary embedding and the layout change in
+    one kernel per part (``flux_dit_glue.cu``)."""
+
+    b = parts[0][0].shape[0]
+    total = sum(x.shape[1] for x, _ in parts)
+    dev = parts[0][0].device
+    q, k, v = (torch.empty((b, heads, total, 128), dtype=torch.bfloat16, device=dev) for _ in range(3))
+    rot_f = torch.view_as_real(rot[:, 0].contiguous())  # (batch, total, 64, 2)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+    off = 0
+    lib = glue()
+    for x, owner in parts:
+        qs = owner.q_norm.scale.to(torch.bfloat16)
+        ks = owner.k_norm.scale.to(torch.bfloat16)
+        rc = lib.flux_qk_norm_rope(x.data_ptr(), x.stride(1), b, x.shape[1], heads, qs.data_ptr(), ks.data_ptr(),
+                                   1e-6, rot_f.data_ptr(), off, total, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                   stream)
+        if rc != 0:
+            raise RuntimeError(f"flux_qk_norm_rope failed ({rc})")
+        off += x.shape[1]
+    o = F.scaled_dot_product_attention(q, k, v)
+    return o.transpose(1, 2).flatten(2)
+
+
+def _use_glue(flags, x) -> bool:
+    return flags.get("fuse_attention_glue", False) and x.is_cuda and x.dtype == torch.bfloat16 and glue() is not None
+
+
 class DoubleStreamBlock(nn.Module):
     """Image and text tokens keep separate weights and join for attention."""
 
@@ -160,9 +226,14 @@ class DoubleStreamBlock(nn.Module):
 
     def forward(self, img, txt, vec, rot):
         im, tm = self.img_mod(vec), self.txt_mod(vec)
-        tq, tk, tv = self.txt_attn.qkv_heads(modulated_linear(self.flags, self.txt_attn.qkv, txt, tm[0], tm[1]))
-        iq, ik, iv = self.img_attn.qkv_heads(modulated_linear(self.flags, self.img_attn.qkv, img, im[0], im[1]))
-        a = attend(torch.cat((tq, iq), 2), torch.cat((tk, ik), 2), torch.cat((tv, iv), 2), rot)
+        t_qkv = modulated_linear(self.flags, self.txt_attn.qkv, txt, tm[0], tm[1])
+        i_qkv = modulated_linear(self.flags, self.img_attn.qkv, img, im[0], im[1])
+        if _use_glue(self.flags, t_qkv):
+            a = fused_attention_inputs([(t_qkv, self.txt_attn), (i_qkv, self.img_attn)], rot, self.txt_attn.heads)
+        else:
+            tq, tk, tv = self.txt_attn.qkv_heads(t_qkv)
+            iq, ik, iv = self.img_attn.qkv_heads(i_qkv)
+            a = attend(torch.cat((tq, iq), 2), torch.cat((tk, ik), 2), torch.cat((tv, iv), 2), rot)
         n_txt = txt.shape[1]
         txt = torch.addcmul(txt, tm[2], self.txt_attn.proj(a[:, :n_txt]))
         img = torch.addcmul(img, im[2], self.img_attn.proj(a[:, n_txt:]))
@@ -187,8 +258,11 @@ class SingleStreamBlock(nn.Module):
         shift, scale, gate = self.modulation(vec)
         h = modulated_linear(self.flags, self.linear1, x, shift, scale)
         qkv, m = h.split((3 * self.width, self.mlp), dim=-1)
-        q, k, v = split_heads(qkv, self.heads)
-        a = attend(self.q_norm(q), self.k_norm(k), v, rot)
+        if _use_glue(self.flags, h):
+            a = fused_attention_inputs([(h, self)], rot, self.heads)
+        else:
+            q, k, v = split_heads(qkv, self.heads)
+            a = attend(self.q_norm(q), self.k_norm(k), v, rot)
         return torch.addcmul(x, gate, self.linear2(torch.cat((a, self.act(m)), dim=-1)))
 
 
@@ -201,7 +275,7 @@ class FluxDiT(nn.Module):
         width, heads = cfg["hidden"], cfg["heads"]
         mlp = int(width * cfg["mlp_ratio"])
         self.cfg = cfg
-        self.flags = {"fuse_modulated_norm": False}
+        self.flags = {"fuse_modulated_norm": False, "fuse_attention_glue": False}
         self.img_in = nn.Linear(cfg["in_channels"], width)
         self.time_in = Embedder(256, width)
         self.guidance_in = Embedder(256, width)
@@ -213,6 +287,14 @@ class FluxDiT(nn.Module):
             [SingleStreamBlock(width, heads, mlp, self.flags) for _ in range(cfg["depth_single"])])
         self.final_mod = Modulation(width, 2)
         self.final_linear = nn.Linear(width, cfg["in_channels"])
+
+    @property
+    def fuse_attention_glue(self) -> bool:
+        return self.flags["fuse_attention_glue"]
+
+    @fuse_attention_glue.setter
+    def fuse_attention_glue(self, on: bool) -> None:
+        self.flags["fuse_attention_glue"] = bool(on)
 
     @property
     def fuse_modulated_norm(self) -> bool:

@@ -89,3 +89,45 @@ def test_fused_modulated_norm_codes_inside_the_dit(monkeypatch):
     assert max(s[1] for s in stats) <= 1e-3, stats
     assert max(s[2] for s in stats) <= 2.0 ** -7, stats
     assert_no_device_error()
+
+
+def test_attention_glue_tracks_torch_ops():
+    # q/k RMSNorm + rotary + attention layout in one kernel, against the torch
+    # ops it replaces: the two streams side by side, and a single-block row
+    # with extra MLP columns (row stride > 3 heads x 128)
+    flux_dit.build_glue()
+    g = torch.Generator(device=dev()).manual_seed(11)
+    b, heads, lt, li = 2, 4, 24, 40
+    ids = torch.zeros((b, lt + li, 3), device=dev())
+    ids[:, lt:, 1] = torch.arange(li, device=dev()).float() // 8
+    ids[:, lt:, 2] = torch.arange(li, device=dev()).float() % 8
+    rot = flux_dit.rotary_tables(ids, (16, 56, 56), 10000)
+    owners = [flux_dit.Attention(heads * 128, heads).to(dev()), flux_dit.Attention(heads * 128, heads).to(dev())]
+    for o in owners:
+        o.q_norm.scale.data = (1 + 0.1 * torch.randn(128, generator=g, device=dev())).to(torch.bfloat16)
+        o.k_norm.scale.data = (1 + 0.1 * torch.randn(128, generator=g, device=dev())).to(torch.bfloat16)
+    t_qkv = torch.randn((b, lt, 3 * heads * 128), generator=g, device=dev()).to(torch.bfloat16)
+    wide = torch.randn((b, li, 3 * heads * 128 + 256), generator=g, device=dev()).to(torch.bfloat16)
+    i_qkv = wide[..., : 3 * heads * 128]
+    with torch.no_grad():
+        got = flux_dit.fused_attention_inputs([(t_qkv, owners[0]), (wide, owners[1])], rot, heads).float()
+        tq, tk, tv = owners[0].qkv_heads(t_qkv)
+        iq, ik, iv = owners[1].qkv_heads(i_qkv)
+        want = flux_dit.attend(torch.cat((tq, iq), 2), torch.cat((tk, ik), 2), torch.cat((tv, iv), 2), rot).float()
+    rel = float((got - want).norm() / want.norm())
+    assert rel < 5e-3, rel
+
+
+def test_dense_dit_with_attention_glue_tracks_torch_ops():
+    model = flux_dit.build_flux_dit(dev(), 12, TINY)
+    img, txt, y, ids = flux_dit.dit_inputs(2, dev(), 13, TINY, img_tokens=64, txt_tokens=32)
+    t = torch.tensor([0.4, 0.9], device=dev())
+    guide = torch.full((2,), 3.5, device=dev())
+    flux_dit.build_glue()
+    with torch.no_grad():
+        rot = model.rotary(ids)
+        want = model(img, txt, rot, t, y, guide).float()
+        model.fuse_attention_glue = True
+        got = model(img, txt, rot, t, y, guide).float()
+    rel = float((got - want).norm() / want.norm())
+    assert rel < 2e-2, rel

@@ -63,6 +63,8 @@ def glue():
         P, I64 = ctypes.c_void_p, ctypes.c_int64
         lib.flux_qk_norm_rope.argtypes = [P, I64, I64, I64, I64, P, P, ctypes.c_float, P, I64, I64, P, P, P, P]
         lib.flux_qk_norm_rope.restype = ctypes.c_int
+        lib.flux_gelu_concat.argtypes = [P, I64, P, I64, I64, I64, I64, P, P]
+        lib.flux_gelu_concat.restype = ctypes.c_int
         _glue = lib
     return _glue
 
@@ -205,6 +207,20 @@ def fused_attention_inputs(parts, rot, heads):
     return o.transpose(1, 2).flatten(2)
 
 
+def gelu_concat(a: torch.Tensor, m: torch.Tensor) -> torch.Tensor:
+    """``torch.cat((a, gelu_tanh(m)), -1)`` in one kernel; m may be a column
+    slice of a wider tensor (rows of a fixed stride)."""
+
+    b, n = a.shape[0], a.shape[1]
+    out = torch.empty((b, n, a.shape[2] + m.shape[2]), dtype=torch.bfloat16, device=a.device)
+    stream = ctypes.c_void_p(torch.cuda.current_stream(a.device).cuda_stream)
+    rc = glue().flux_gelu_concat(a.data_ptr(), a.stride(1), m.data_ptr(), m.stride(1), b * n, a.shape[2], m.shape[2],
+                                 out.data_ptr(), stream)
+    if rc != 0:
+        raise RuntimeError(f"flux_gelu_concat failed ({rc})")
+    return out
+
+
 def _use_glue(flags, x) -> bool:
     return flags.get("fuse_attention_glue", False) and x.is_cuda and x.dtype == torch.bfloat16 and glue() is not None
 
@@ -260,9 +276,9 @@ class SingleStreamBlock(nn.Module):
         qkv, m = h.split((3 * self.width, self.mlp), dim=-1)
         if _use_glue(self.flags, h):
             a = fused_attention_inputs([(h, self)], rot, self.heads)
-        else:
-            q, k, v = split_heads(qkv, self.heads)
-            a = attend(self.q_norm(q), self.k_norm(k), v, rot)
+            return torch.addcmul(x, gate, self.linear2(gelu_concat(a, m)))
+        q, k, v = split_heads(qkv, self.heads)
+        a = attend(self.q_norm(q), self.k_norm(k), v, rot)
         return torch.addcmul(x, gate, self.linear2(torch.cat((a, self.act(m)), dim=-1)))
 
 

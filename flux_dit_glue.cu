@@ -72,7 +72,57 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       *reinterpret_cast<const uint2*>(row + (2 * heads + h) * kDim + 4 * lane);
 }
 
+// out row r = [a[r, 0:da], gelu_tanh(m[r, 0:dm])]: the input of a single
+// block's output projection, with the MLP half's activation applied on the
+// way (float32 math, one bf16 rounding, as torch's tanh-approximated GELU).
+// 8 elements (16 bytes) per thread; da and dm multiples of 8.
+__global__ void __launch_bounds__(256) gelu_concat_kernel(const __nv_bfloat16* __restrict__ a, int64_t a_stride,
+                                                         const __nv_bfloat16* __restrict__ m, int64_t m_stride,
+                                                         int64_t rows, int da, int dm,
+                                                         __nv_bfloat16* __restrict__ out) {
+  const int vecs = (da + dm) / 8;
+  const int64_t total = rows * vecs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / vecs;
+    const int c = static_cast<int>(i % vecs) * 8;
+    uint4 v;
+    if (c < da) {
+      v = *reinterpret_cast<const uint4*>(a + r * a_stride + c);
+    } else {
+      const uint4 x = *reinterpret_cast<const uint4*>(m + r * m_stride + (c - da));
+      const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+      uint32_t yw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[j]));
+        const float g0 = 0.5f * f.x * (1.0f + tanhf(0.7978845608028654f * (f.x + 0.044715f * f.x * f.x * f.x)));
+        const float g1 = 0.5f * f.y * (1.0f + tanhf(0.7978845608028654f * (f.y + 0.044715f * f.y * f.y * f.y)));
+        const __nv_bfloat162 y = __floats2bfloat162_rn(g0, g1);
+        yw[j] = *reinterpret_cast<const uint32_t*>(&y);
+      }
+      v = make_uint4(yw[0], yw[1], yw[2], yw[3]);
+    }
+    *reinterpret_cast<uint4*>(out + r * (da + dm) + c) = v;
+  }
+}
+
 }  // namespace
+
+extern "C" int flux_gelu_concat(const void* a, int64_t a_stride, const void* m, int64_t m_stride, int64_t rows,
+                                int64_t da, int64_t dm, void* out, void* stream) {
+  if (rows == 0) return 0;
+  if (rows < 0 || da % 8 || dm % 8 || a_stride % 8 || m_stride % 8) return -1;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(out)) % 16)
+    return -1;
+  int sms = 148;
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  gelu_concat_kernel<<<sms * 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(a), a_stride, static_cast<const __nv_bfloat16*>(m), m_stride, rows,
+      static_cast<int>(da), static_cast<int>(dm), static_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 
 extern "C" int flux_qk_norm_rope(const void* qkv, int64_t row_stride, int64_t batch, int64_t tokens, int64_t heads,
                                  const void* q_scale, const void* k_scale, float eps, const void* rot, int64_t l_off,

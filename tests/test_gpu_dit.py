@@ -131,3 +131,17 @@ def test_dense_dit_with_attention_glue_tracks_torch_ops():
         got = model(img, txt, rot, t, y, guide).float()
     rel = float((got - want).norm() / want.norm())
     assert rel < 2e-2, rel
+
+
+def test_gelu_concat_tracks_torch_ops():
+    flux_dit.build_glue()
+    g = torch.Generator(device=dev()).manual_seed(14)
+    a = torch.randn((2, 33, 512), generator=g, device=dev()).to(torch.bfloat16)
+    h = (torch.randn((2, 33, 3 * 512 + 2048), generator=g, device=dev()) * 3).to(torch.bfloat16)
+    m = h[..., 3 * 512:]
+    got = flux_dit.gelu_concat(a, m).float()
+    want = torch.cat((a, torch.nn.functional.gelu(m, approximate="tanh")), dim=-1).float()
+    assert torch.equal(got[..., :512], want[..., :512])
+    diff = (got - want).abs()
+    assert float(diff.max()) <= float(want.abs().max()) * 2.0 ** -7  # within one bf16 ulp of the largest value
+    assert float((diff != 0).float().mean()) < 0.05

@@ -37,6 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "convrot_prepare_packed": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _P]),
     "convrot_rotate": (_I, [_P, _I, _I64, _I64, _I, _P, _P]),
     "convrot_modnorm_prepare_i8": (_I, [_P, _I, _I64, _I64, _I, _P, _P, _I64, _I64, ctypes.c_float, _P, _P, _P]),
+    "convrot_gelu_concat_prepare_i8": (_I, [_P, _I64, _I64, _P, _I64, _I64, _I64, _I, _P, _P, _P]),
     "convrot_unpack_int4": (_I, [_P, _I64, _P, _P]),
     "convrot_pack_int4": (_I, [_P, _I64, _P, _P]),
     "convrot_repack_int4_transpose": (_I, [_P, _I64, _I64, _P, _P]),

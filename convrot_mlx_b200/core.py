@@ -320,6 +320,37 @@ def modulated_norm_prepare_i8(x: torch.Tensor, shift: torch.Tensor, scale: torch
     return codes, scales
 
 
+def gelu_concat_prepare_i8(a: torch.Tensor, m: torch.Tensor,
+                           group_size: int = CONVROT_GROUP_SIZE) -> tuple[torch.Tensor, torch.Tensor]:
+    """int8 codes and row scales of ``prepare(cat(a, gelu_tanh(m), -1))`` in one
+    kernel (``convrot_gelu_concat_prepare_i8``), reading a and m in place: a
+    (batch, tokens, da) and m (batch, tokens, dm) bf16, each with unit stride
+    along its last dimension (m may be a column slice of a wider tensor)."""
+
+    _require_cuda(a, m)
+    if a.dtype != torch.bfloat16 or m.dtype != torch.bfloat16:
+        raise ValueError("the fused GELU-concatenation prep takes bfloat16 tensors")
+    if a.shape[:-1] != m.shape[:-1]:
+        raise ValueError(f"leading shapes differ: {tuple(a.shape)} and {tuple(m.shape)}")
+    da, dm = a.shape[-1], m.shape[-1]
+    a2 = a.reshape(-1, da)
+    m2 = m.reshape(-1, dm)
+    if a2.stride(-1) != 1 or a2.stride(0) % 8 or a2.data_ptr() % 16:
+        a2 = a2.contiguous()
+    if m2.stride(-1) != 1 or m2.stride(0) % 8 or m2.data_ptr() % 16:
+        m2 = m2.contiguous()
+    rows = a2.shape[0]
+    codes = torch.empty((rows, da + dm), dtype=torch.int8, device=a.device)
+    scales = torch.empty((rows,), dtype=torch.float32, device=a.device)
+    _lib.check(
+        _lib.load().convrot_gelu_concat_prepare_i8(
+            _lib.ptr(a2), a2.stride(0), da, _lib.ptr(m2), m2.stride(0), dm, rows, group_size, _lib.ptr(codes),
+            _lib.ptr(scales), _lib.stream_of(a2)),
+        "GELU-concatenation activation preparation",
+    )
+    return codes, scales
+
+
 # ---------------------------------------------------------------------------
 # GEMMs
 
@@ -615,6 +646,26 @@ class ConvRotLinear(nn.Module):
         m = codes.shape[0]
         out = _gemm_w4a4(codes, self.qweight, self.layout_code, xscales, self.scales, self.bias, x.dtype,
                          m, self.out_features, self.in_features)
+        return out.reshape(*lead, self.out_features)
+
+    def forward_gelu_concat(self, a: torch.Tensor, m: torch.Tensor) -> torch.Tensor:
+        """``self(torch.cat((a, gelu_tanh(m)), -1))`` with the GELU, the
+        concatenation, the rotation and the A4 quantization in one kernel
+        (``gelu_concat_prepare_i8``), then the W4A4 GEMM: the output
+        projection of a FLUX single block.  An extension with no counterpart
+        in the reference; the W4A16 backend and other dtypes take the
+        unfused path."""
+
+        lead = a.shape[:-1]
+        if a.shape[-1] + m.shape[-1] != self.in_features:
+            raise ValueError(f"ConvRotLinear expected K={self.in_features}, got {a.shape[-1]} + {m.shape[-1]}")
+        if (self.backend == "mpp-w4a16" or a.dtype != torch.bfloat16 or self.group_size not in (64, 256)
+                or a.shape[-1] % 16):
+            gelu = torch.nn.functional.gelu(m, approximate="tanh")
+            return self(torch.cat((a, gelu), dim=-1))
+        codes, xscales = gelu_concat_prepare_i8(a, m, self.group_size)
+        out = _gemm_w4a4(codes, self.qweight, self.layout_code, xscales, self.scales, self.bias, a.dtype,
+                         codes.shape[0], self.out_features, self.in_features)
         return out.reshape(*lead, self.out_features)
 
     def extra_repr(self) -> str:

@@ -21,6 +21,13 @@
 // Only step 1's summation order is this kernel's own: a last-bit difference in
 // the mean or rstd can move a y or xm across a bf16 rounding boundary, and a
 // code then by one.
+//
+// The same kernel serves a second producer: the input of a FLUX single
+// block's output projection, cat(a, gelu_tanh(m)) -- the attention output
+// and the MLP half of the block's fused input projection, a column slice of a
+// wider tensor.  Then each row is read from its two sources, the GELU is
+// applied on load (float32, explicit roundings, one bf16 rounding), and steps
+// 1-2 are skipped: the codes are bit for bit prepare_i8 of the concatenation.
 #include "prep_impl.cuh"
 
 namespace convrot {
@@ -29,13 +36,55 @@ namespace {
 using bf16 = __nv_bfloat16;
 using bf162 = __nv_bfloat162;
 
+constexpr int kSrcModNorm = 0, kSrcGeluCat = 1;
+
 struct ModNorm {
   const bf16* shift;   // (samples, features) with row stride mod_stride
   const bf16* scale;
   int64_t rows_per_mod;  // rows (tokens) per sample
   int64_t mod_stride;    // elements between consecutive samples' vectors
   float eps;
+  // kSrcGeluCat: row r = [a[r, 0:da], gelu(m[r, 0:K - da])], a = x
+  const bf16* m;
+  int64_t a_stride, m_stride;
+  int da;
 };
+
+// tanh-approximated GELU in float32 with every rounding spelled out (so that
+// no compiler contraction changes it): 0.5 x (1 + tanh(c (x + 0.044715 x^3)))
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
+__device__ __forceinline__ void gelu16(Raw16<bf16>& r) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t* w = reinterpret_cast<uint32_t*>(&r.v[q]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const bf162*>(&w[i]));
+      const bf162 g = __floats2bfloat162_rn(gelu_tanh(f.x), gelu_tanh(f.y));
+      w[i] = *reinterpret_cast<const uint32_t*>(&g);
+    }
+  }
+}
+
+// 16 consecutive elements of a row starting at column c (c and da multiples
+// of 16, so a unit never straddles the two sources)
+template <int SRC>
+__device__ __forceinline__ void load_unit(Raw16<bf16>& r, const bf16* x, const ModNorm& mn, int64_t row, int K,
+                                          int c) {
+  if constexpr (SRC == kSrcModNorm) {
+    load16(r, x + row * static_cast<int64_t>(K) + c);
+  } else if (c < mn.da) {
+    load16(r, x + row * mn.a_stride + c);
+  } else {
+    load16(r, mn.m + row * mn.m_stride + (c - mn.da));
+    gelu16(r);
+  }
+}
 
 __device__ __forceinline__ float block_sum(float v, float* red, int tid, int nthr) {
 #pragma unroll
@@ -118,7 +167,7 @@ __device__ __forceinline__ float sumsq16(const Raw16<bf16>& r, float mean) {
 
 // One CTA per row; the rotation and quantization below follow prep_kernel's
 // unstaged bf16 path (fast quantizer, int8 codes) step for step.
-template <int G, int UPT>
+template <int G, int UPT, int SRC>
 __global__ void __launch_bounds__(256) modnorm_prep_kernel(const bf16* __restrict__ x, int64_t rows, int K, int half,
                                                              const ModNorm mn, int8_t* __restrict__ out,
                                                              float* __restrict__ scales) {
@@ -145,21 +194,21 @@ __global__ void __launch_bounds__(256) modnorm_prep_kernel(const bf16* __restric
   grid_dependents_launch();
 
   for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const bf16* xr = x + row * static_cast<int64_t>(K);
-    const int64_t sample = row / mn.rows_per_mod;
-    const bf16* shift = mn.shift + sample * mn.mod_stride;
-    const bf16* scale = mn.scale + sample * mn.mod_stride;
     Raw16<bf16> rlo[UPT], rhi[UPT];
 #pragma unroll
     for (int j = 0; j < UPT; ++j) {
       const int u = tid + j * nthr;
       if (u < units) {
         const int p0 = u << 4;
-        load16(rlo[j], xr + p0);
-        if (p0 + half < K) load16(rhi[j], xr + p0 + half);
+        load_unit<SRC>(rlo[j], x, mn, row, K, p0);
+        if (p0 + half < K) load_unit<SRC>(rhi[j], x, mn, row, K, p0 + half);
         else zero16(rhi[j]);
       }
     }
+    if constexpr (SRC == kSrcModNorm) {
+    const int64_t sample = row / mn.rows_per_mod;
+    const bf16* shift = mn.shift + sample * mn.mod_stride;
+    const bf16* scale = mn.scale + sample * mn.mod_stride;
     // 1. row statistics (float32, two passes over the registers)
     float s = 0.0f;
 #pragma unroll
@@ -187,6 +236,7 @@ __global__ void __launch_bounds__(256) modnorm_prep_kernel(const bf16* __restric
         if (p0 + half < K) modulate16(rhi[j], p0 + half, mean, rstd, shift, scale);
       }
     }
+    }  // kSrcModNorm
     // 3. rotate (strides 1 and 4 in registers, 16 and 64 over shared memory)
 #pragma unroll
     for (int j = 0; j < UPT; ++j) {
@@ -244,7 +294,7 @@ __global__ void __launch_bounds__(256) modnorm_prep_kernel(const bf16* __restric
   }
 }
 
-template <int G>
+template <int G, int SRC>
 int launch_modnorm(const bf16* x, int64_t rows, int K, int half, const ModNorm& mn, int8_t* out, float* scales,
                    cudaStream_t stream) {
   const int units = half / 16;
@@ -267,12 +317,12 @@ int launch_modnorm(const bf16* x, int64_t rows, int K, int half, const ModNorm& 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, x, rows, K, half, mn, out, scales));
-    return check_launch("convrot modulated-norm prep kernel");
+    return check_launch("convrot fused-producer prep kernel");
   };
   switch (upt) {
-    case 1: return run(modnorm_prep_kernel<G, 1>);
-    case 2: return run(modnorm_prep_kernel<G, 2>);
-    default: return run(modnorm_prep_kernel<G, 4>);
+    case 1: return run(modnorm_prep_kernel<G, 1, SRC>);
+    case 2: return run(modnorm_prep_kernel<G, 2, SRC>);
+    default: return run(modnorm_prep_kernel<G, 4, SRC>);
   }
 }
 
@@ -309,12 +359,45 @@ int convrot_modnorm_prepare_i8(const void* x, int dtype, int64_t rows, int64_t f
   CONVROT_REQUIRE(half % 16 == 0, CONVROT_ERR_UNSUPPORTED, "unsupported feature count %lld",
                   static_cast<long long>(features));
   ModNorm mn{static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale), rows_per_mod,
-             mod_stride, eps};
+             mod_stride, eps, nullptr, 0, 0, 0};
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int k = static_cast<int>(features), h = static_cast<int>(half);
-  if (group_size == 64) return launch_modnorm<64>(xb, rows, k, h, mn, q_i8, scales, s);
-  return launch_modnorm<256>(xb, rows, k, h, mn, q_i8, scales, s);
+  if (group_size == 64) return launch_modnorm<64, kSrcModNorm>(xb, rows, k, h, mn, q_i8, scales, s);
+  return launch_modnorm<256, kSrcModNorm>(xb, rows, k, h, mn, q_i8, scales, s);
+}
+
+int convrot_gelu_concat_prepare_i8(const void* a, int64_t a_stride, int64_t da, const void* m, int64_t m_stride,
+                                   int64_t dm, int64_t rows, int group_size, int8_t* q_i8, float* scales,
+                                   void* stream) {
+  using namespace convrot;
+  const int64_t features = da + dm;
+  CONVROT_REQUIRE(group_size == 64 || group_size == 256, CONVROT_ERR_UNSUPPORTED,
+                  "the GELU-concatenation prep covers groups 64 and 256, got %d", group_size);
+  CONVROT_REQUIRE(rows >= 0 && da > 0 && dm > 0 && features % group_size == 0, CONVROT_ERR_INVALID,
+                  "invalid shape: rows %lld, widths %lld + %lld for group %d", static_cast<long long>(rows),
+                  static_cast<long long>(da), static_cast<long long>(dm), group_size);
+  CONVROT_REQUIRE(da % 16 == 0, CONVROT_ERR_UNSUPPORTED, "the first part's width must be a multiple of 16, got %lld",
+                  static_cast<long long>(da));
+  CONVROT_REQUIRE(a_stride >= da && m_stride >= dm && a_stride % 8 == 0 && m_stride % 8 == 0, CONVROT_ERR_INVALID,
+                  "row strides must cover the widths and be multiples of 8 elements (%lld, %lld)",
+                  static_cast<long long>(a_stride), static_cast<long long>(m_stride));
+  CONVROT_REQUIRE(features <= (1 << 20), CONVROT_ERR_UNSUPPORTED, "features too large");
+  if (rows == 0) return CONVROT_OK;
+  CONVROT_REQUIRE(a && m && q_i8 && scales, CONVROT_ERR_INVALID, "null pointer");
+  CONVROT_REQUIRE(aligned_to(a, 16) && aligned_to(m, 16) && aligned_to(q_i8, 16), CONVROT_ERR_INVALID,
+                  "a, m and the codes must be 16-byte aligned");
+  const int64_t groups = features / group_size;
+  const int64_t half = ((groups + 1) / 2) * group_size;
+  CONVROT_REQUIRE(half % 16 == 0, CONVROT_ERR_UNSUPPORTED, "unsupported feature count %lld",
+                  static_cast<long long>(features));
+  ModNorm mn{nullptr, nullptr, 1, 0, 0.0f, static_cast<const __nv_bfloat16*>(m), a_stride, m_stride,
+             static_cast<int>(da)};
+  const auto* ab = static_cast<const __nv_bfloat16*>(a);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int k = static_cast<int>(features), h = static_cast<int>(half);
+  if (group_size == 64) return launch_modnorm<64, kSrcGeluCat>(ab, rows, k, h, mn, q_i8, scales, s);
+  return launch_modnorm<256, kSrcGeluCat>(ab, rows, k, h, mn, q_i8, scales, s);
 }
 
 }  // extern "C"

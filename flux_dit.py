@@ -21,7 +21,15 @@ first MLP projections of both streams and the single blocks' fused
 projection -- and the linear is a ``ConvRotLinear`` with
 ``fuse_modulated_norm`` set on the model, the norm, the modulation, the
 rotation and the A4 quantization run as one kernel
-(``ConvRotLinear.forward_modulated_norm``).
+(``ConvRotLinear.forward_modulated_norm``); with the attention glue on as
+well, the single blocks' output projection likewise quantizes
+cat(attention, gelu(mlp)) straight from its two parts
+(``ConvRotLinear.forward_gelu_concat``).
+
+``fuse_attention_glue`` (both arms of the benchmark) runs the q/k RMSNorm,
+the rotary embedding and the attention layout of q, k, v as one kernel, and
+the single blocks' GELU with the concatenation after attention as another
+(``flux_dit_glue.cu``, built by ``build_glue``).
 """
 
 from __future__ import annotations
@@ -276,6 +284,9 @@ class SingleStreamBlock(nn.Module):
         qkv, m = h.split((3 * self.width, self.mlp), dim=-1)
         if _use_glue(self.flags, h):
             a = fused_attention_inputs([(h, self)], rot, self.heads)
+            fused = getattr(self.linear2, "forward_gelu_concat", None)
+            if fused is not None and self.flags.get("fuse_modulated_norm", False):
+                return torch.addcmul(x, gate, fused(a, m))
             return torch.addcmul(x, gate, self.linear2(gelu_concat(a, m)))
         q, k, v = split_heads(qkv, self.heads)
         a = attend(self.q_norm(q), self.k_norm(k), v, rot)

@@ -72,6 +72,15 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
       *reinterpret_cast<const uint2*>(row + (2 * heads + h) * kDim + 4 * lane);
 }
 
+// tanh-approximated GELU in float32 with every rounding spelled out, the
+// form the fused W4A4 prep of the same concatenation uses
+// (convrot_gelu_concat_prepare_i8), so both give the same bits
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(0.7978845608028654f, __fadd_rn(x, __fmul_rn(0.044715f, x3)));
+  return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+}
+
 // out row r = [a[r, 0:da], gelu_tanh(m[r, 0:dm])]: the input of a single
 // block's output projection, with the MLP half's activation applied on the
 // way (float32 math, one bf16 rounding, as torch's tanh-approximated GELU).
@@ -96,9 +105,7 @@ __global__ void __launch_bounds__(256) gelu_concat_kernel(const __nv_bfloat16* _
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xw[j]));
-        const float g0 = 0.5f * f.x * (1.0f + tanhf(0.7978845608028654f * (f.x + 0.044715f * f.x * f.x * f.x)));
-        const float g1 = 0.5f * f.y * (1.0f + tanhf(0.7978845608028654f * (f.y + 0.044715f * f.y * f.y * f.y)));
-        const __nv_bfloat162 y = __floats2bfloat162_rn(g0, g1);
+        const __nv_bfloat162 y = __floats2bfloat162_rn(gelu_tanh(f.x), gelu_tanh(f.y));
         yw[j] = *reinterpret_cast<const uint32_t*>(&y);
       }
       v = make_uint4(yw[0], yw[1], yw[2], yw[3]);

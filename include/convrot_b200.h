@@ -108,6 +108,23 @@ int convrot_modnorm_prepare_i8(const void* x, int dtype, int64_t rows, int64_t f
                                float eps, int8_t* q_i8, float* scales, void* stream);
 
 /*
+ * The prep of a FLUX single block's output-projection input fused into its
+ * producer: the int8 codes and row scales of convrot_prepare_i8 applied to
+ * row r = [a[r, 0:da], gelu_tanh(m[r, 0:dm])] -- the attention output and
+ * the MLP half of the block's input projection -- read straight from the two
+ * tensors (row strides a_stride and m_stride elements, multiples of 8;
+ * da % 16 == 0).  gelu_tanh(x) = 0.5 x (1 + tanh(0.7978845608028654 (x +
+ * 0.044715 x^3))) in float32 with each product and sum rounded separately,
+ * then one bf16 rounding.  bfloat16 only; group_size 64 or 256.  Bit for bit
+ * convrot_prepare_i8 of the concatenated row.  No reference counterpart: the
+ * same fusion of the preparation pass into the producing op as
+ * convrot_modnorm_prepare_i8.
+ */
+int convrot_gelu_concat_prepare_i8(const void* a, int64_t a_stride, int64_t da, const void* m, int64_t m_stride,
+                                   int64_t dm, int64_t rows, int group_size, int8_t* q_i8, float* scales,
+                                   void* stream);
+
+/*
  * Packed int4 -> int8.  Replaces metal_unpack_signed_int4 (core.py:1014-1027;
  * Metal kernel core.py:915-922) and unpack_signed_int4 (core.py:108-120).
  * packed: n_bytes bytes; out: 2 * n_bytes int8 values in [-8, 7].

@@ -12,6 +12,9 @@
   summation order): codes are compared with the oracle of a float64
   LayerNorm, at most 0.1% differing and none by more than one; the layer's
   bf16 output stays within rel-L2 1e-3 of the unfused torch path.
+* The same kernel fed by a FLUX single block's cat(attention, gelu(mlp))
+  (convrot_gelu_concat_prepare_i8, ConvRotLinear.forward_gelu_concat) is
+  bit for bit prepare_i8 of the concatenation.
 """
 
 from __future__ import annotations
@@ -129,4 +132,48 @@ def test_fused_prep_argument_errors():
     with pytest.raises(ValueError):
         modulated_norm_prepare_i8(x.float(), s, s)
     torch.cuda.synchronize()
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("group", [64, 256])
+@pytest.mark.parametrize("da,dm", [(3072, 12288), (512, 2048)])
+def test_gelu_concat_prep_equals_prep_of_the_concatenation(group, da, dm):
+    # the single-block output projection's input, cat(attention, gelu(mlp half
+    # of a wider tensor)): fused, it must give exactly prepare_i8 of the
+    # concatenation built by the DiT's glue kernel (the same GELU form)
+    import flux_dit
+    from convrot_mlx_b200.core import gelu_concat_prepare_i8
+
+    flux_dit.build_glue()
+    g = torch.Generator(device=dev()).manual_seed(da + group)
+    a = torch.randn((2, 37, da), generator=g, device=dev()).to(torch.bfloat16)
+    h = (torch.randn((2, 37, 3 * da + dm), generator=g, device=dev()) * 2.5).to(torch.bfloat16)
+    m = h[..., 3 * da:]
+    codes, scales = gelu_concat_prepare_i8(a, m, group)
+    cat = flux_dit.gelu_concat(a, m)
+    want_c, want_s = cr.metal_fused_prepare_convrot_activation_i8(cat.reshape(-1, da + dm), group)
+    assert torch.equal(codes, want_c)
+    assert torch.equal(scales, want_s)
+    assert_no_device_error()
+
+
+def test_layer_forward_gelu_concat_equals_unfused():
+    import flux_dit
+
+    flux_dit.build_glue()
+    da, dm, n = 512, 2048, 512
+    g = torch.Generator(device=dev()).manual_seed(21)
+    w = (torch.randn((n, da + dm), generator=g, device=dev()) * 0.02).to(torch.bfloat16)
+    layer = cr.ConvRotLinear(da + dm, n, device=dev())
+    qnk, ws = cr.quantize_convrot_weight(w)
+    layer.qweight, layer.scales = cr.repack_nk_weight_for_mpp(qnk), ws
+    layer.bias = torch.randn((n,), generator=g, device=dev()) * 0.01
+    a = torch.randn((3, 50, da), generator=g, device=dev()).to(torch.bfloat16)
+    h = torch.randn((3, 50, 3 * da + dm), generator=g, device=dev()).to(torch.bfloat16)
+    got = layer.forward_gelu_concat(a, h[..., 3 * da:])
+    want = layer(flux_dit.gelu_concat(a, h[..., 3 * da:]))
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+    # and within bf16 rounding of torch's own tanh GELU
+    ref = layer(torch.cat((a, torch.nn.functional.gelu(h[..., 3 * da:], approximate="tanh")), -1)).float()
+    assert float((got.float() - ref).norm() / ref.norm()) < 1e-2
     assert_no_device_error()

@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "convrot_w4a4_gemm_gather": (_I, [_P, _P, _I, _P, _P, _P, ctypes.POINTER(_P), _I, _I64, _I64, _I, _I64, _I64,
                                       _I64, _P]),
     "convrot_peer_barrier": (_I, [ctypes.POINTER(_P), _I, _I, ctypes.c_uint32, _P]),
+    "convrot_copy_2d": (_I, [_P, _I64, _P, _I64, _I64, _I64, _P]),
     "convrot_w4a4_linear_static": (_I, [_P, _I, _I, _P, _I, _P, _P, _P, _I, _I64, _I64, _I64, _P]),
     "convrot_set_gemm_route": (_I, [_I]),
     "convrot_take_device_error": (_I, [ctypes.POINTER(_I)]),

@@ -59,4 +59,24 @@ int convrot_peer_barrier(uint32_t* const* flag_arrays, int world, int rank, uint
   return check_launch("convrot peer barrier");
 }
 
+// One strided block copy on a copy engine: `rows` rows of `width_bytes`,
+// source rows `src_pitch` bytes apart, destination rows `dst_pitch` apart.
+// The tensor-parallel layer pushes each M-chunk of its column shard into
+// every peer's output with it (peer memory mapped into this GPU), so the
+// gather runs on the copy engines while the SMs compute the next chunk.
+int convrot_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width_bytes,
+                    int64_t rows, void* stream) {
+  using namespace convrot;
+  CONVROT_REQUIRE(rows >= 0 && width_bytes >= 0 && dst_pitch >= width_bytes && src_pitch >= width_bytes,
+                  CONVROT_ERR_INVALID, "invalid 2-D copy: %lld rows of %lld bytes, pitches %lld / %lld",
+                  static_cast<long long>(rows), static_cast<long long>(width_bytes),
+                  static_cast<long long>(dst_pitch), static_cast<long long>(src_pitch));
+  if (rows == 0 || width_bytes == 0) return CONVROT_OK;
+  CONVROT_REQUIRE(dst && src, CONVROT_ERR_INVALID, "null pointer");
+  CONVROT_CUDA_CHECK(cudaMemcpy2DAsync(dst, static_cast<size_t>(dst_pitch), src, static_cast<size_t>(src_pitch),
+                                       static_cast<size_t>(width_bytes), static_cast<size_t>(rows),
+                                       cudaMemcpyDeviceToDevice, static_cast<cudaStream_t>(stream)));
+  return CONVROT_OK;
+}
+
 }  // extern "C"

@@ -6,11 +6,21 @@ GPUs owns output columns ``[r * N / world, (r + 1) * N / world)``: that slice
 of the packed weight (K x packed-N: a column slice of the bytes; N x
 packed-K: a row slice), of the weight scales and of the bias.  The
 activation is replicated and every rank runs the fused rotate + quantize on
-it (cheaper than broadcasting the codes).  The rank's GEMM
-(``convrot_w4a4_gemm_gather``) stores each output tile into every rank's full
-(M, N) output buffer -- its own and, through symmetric memory, its peers' --
-so the all-gather over NVLink overlaps the GEMM; a flag barrier
-(``convrot_peer_barrier``) then makes every rank's full output visible.
+it (cheaper than broadcasting the codes).  Every rank's full (M, N) output
+buffer is symmetric memory, mapped on every GPU, and the all-gather crosses
+NVLink one of two ways:
+
+* ``gather="copy-engine"`` (the default): the GEMM runs in ``chunks`` blocks
+  of rows into this rank's own buffer; after each block one strided copy per
+  peer (``convrot_copy_2d``) pushes it into the peers' buffers on side
+  streams, so the copy engines carry block i while the SMs compute block
+  i + 1.  Measured on B200 for the video-DiT linears, 4.34 ms per step at 4
+  GPUs and 4.26 ms at 2, against 5.10 / 4.38 ms for the epilogue gather.
+* ``gather="epilogue"``: the GEMM's epilogue (``convrot_w4a4_gemm_gather``)
+  stores each output tile into every rank's buffer itself, as peer stores.
+
+Either way a flag barrier (``convrot_peer_barrier``) then makes every rank's
+full output visible.
 
 Buffers are symmetric-memory tensors (``torch.distributed._symmetric_memory``,
 CUDA backend, multicast off) allocated once per (rows, dtype).  Outputs
@@ -76,8 +86,15 @@ class ColumnParallelConvRotLinear(nn.Module):
 
     def __init__(self, in_features: int, out_features: int, *, group: dist.ProcessGroup | None = None,
                  bias: bool = True, group_size: int = CONVROT_GROUP_SIZE, backend: str = "mpp-w4a4",
-                 device=None) -> None:
+                 device=None, gather: str = "copy-engine", chunks: int = 4) -> None:
         super().__init__()
+        if gather not in ("copy-engine", "epilogue"):
+            raise ValueError(f"gather must be 'copy-engine' or 'epilogue', got {gather!r}")
+        if chunks < 1:
+            raise ValueError(f"chunks must be positive, got {chunks}")
+        self.gather = gather
+        self.chunks = chunks
+        self._side = None  # copy-engine gather: one stream per peer
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
         self.rank = dist.get_rank(self.group)
@@ -101,11 +118,13 @@ class ColumnParallelConvRotLinear(nn.Module):
         self._calls = 0     # output buffer = calls % 2
 
     @classmethod
-    def from_full(cls, layer: ConvRotLinear, group: dist.ProcessGroup | None = None) -> "ColumnParallelConvRotLinear":
+    def from_full(cls, layer: ConvRotLinear, group: dist.ProcessGroup | None = None, *, gather: str = "copy-engine",
+                  chunks: int = 4) -> "ColumnParallelConvRotLinear":
         """Shard a full (already quantized) ConvRotLinear on every rank."""
 
         tp = cls(layer.in_features, layer.out_features, group=group, bias=layer.source_has_bias,
-                 group_size=layer.group_size, backend=layer.backend, device=layer.qweight.device)
+                 group_size=layer.group_size, backend=layer.backend, device=layer.qweight.device, gather=gather,
+                 chunks=chunks)
         tp.qweight = shard_weight(layer.qweight, tp.layout, tp.start, tp.stop)
         tp.scales = _f32_vec(layer.scales)[tp.start : tp.stop].clone()
         tp.bias = _f32_vec(layer.bias)[tp.start : tp.stop].clone()
@@ -156,18 +175,65 @@ class ColumnParallelConvRotLinear(nn.Module):
         lib = _lib.load()
         stream = _lib.stream_of(x2d)
         codes, xscales = _prepare(x2d, self.group_size, packed=False)
-        _lib.check(
-            lib.convrot_w4a4_gemm_gather(
-                _lib.ptr(codes), _lib.ptr(self.qweight), self.layout, _lib.ptr(xscales), _lib.ptr(self.scales),
-                _lib.ptr(self.bias), out_ptrs, self.world, self.out_features, self.start, _dtype_code(x.dtype),
-                m, self.shard_features, self.in_features, stream,
-            ),
-            "tensor-parallel W4A4 GEMM",
-        )
+        if self.gather == "epilogue" or self.world == 1:
+            _lib.check(
+                lib.convrot_w4a4_gemm_gather(
+                    _lib.ptr(codes), _lib.ptr(self.qweight), self.layout, _lib.ptr(xscales), _lib.ptr(self.scales),
+                    _lib.ptr(self.bias), out_ptrs, self.world, self.out_features, self.start, _dtype_code(x.dtype),
+                    m, self.shard_features, self.in_features, stream,
+                ),
+                "tensor-parallel W4A4 GEMM",
+            )
+        else:
+            self._gemm_and_copy(lib, codes, xscales, out, out_ptrs, m, x.dtype, stream)
         _lib.check(lib.convrot_peer_barrier(ctypes.cast(flag_ptrs, ctypes.POINTER(ctypes.c_void_p)), self.world,
                                             self.rank, self._epoch, stream), "peer barrier")
         return out.reshape(*lead, self.out_features)
 
+    def _gemm_and_copy(self, lib, codes, xscales, out, out_ptrs, m, dtype, stream) -> None:
+        """The copy-engine gather: the shard GEMM in blocks of rows into this
+        rank's buffer, each block pushed to every peer by a strided copy on a
+        side stream while the next block computes; the current stream then
+        waits for every copy."""
+
+        dev = out.device
+        cur = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = [torch.cuda.Stream(device=dev) for _ in range(self.world)]
+        elt = out.element_size()
+        ldc = self.out_features
+        k = self.in_features
+        rows = -(-m // self.chunks)
+        rows = -(-rows // 256) * 256  # whole 256-row pair tiles
+        own = out.data_ptr()
+        for r0 in range(0, m, rows):
+            mr = min(rows, m - r0)
+            dst = (ctypes.c_void_p * 1)(own + r0 * ldc * elt)
+            _lib.check(
+                lib.convrot_w4a4_gemm_gather(
+                    ctypes.c_void_p(codes.data_ptr() + r0 * k), _lib.ptr(self.qweight), self.layout,
+                    ctypes.c_void_p(xscales.data_ptr() + 4 * r0), _lib.ptr(self.scales), _lib.ptr(self.bias), dst, 1,
+                    ldc, self.start, _dtype_code(dtype), mr, self.shard_features, k, stream,
+                ),
+                "tensor-parallel W4A4 GEMM",
+            )
+            done = torch.cuda.Event()
+            done.record(cur)
+            offset = (r0 * ldc + self.start) * elt
+            for p in range(self.world):
+                if p == self.rank:
+                    continue
+                side = self._side[p]
+                side.wait_event(done)
+                _lib.check(lib.convrot_copy_2d(ctypes.c_void_p(int(out_ptrs[p]) + offset), ldc * elt,
+                                               ctypes.c_void_p(own + offset), ldc * elt, self.shard_features * elt,
+                                               mr, ctypes.c_void_p(side.cuda_stream)), "peer copy")
+        for p in range(self.world):
+            if p != self.rank:
+                copied = torch.cuda.Event()
+                copied.record(self._side[p])
+                cur.wait_event(copied)
+
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, world={self.world}, "
-                f"rank={self.rank}, columns=[{self.start}, {self.stop})")
+                f"rank={self.rank}, columns=[{self.start}, {self.stop}), gather={self.gather}")

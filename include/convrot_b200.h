@@ -210,6 +210,17 @@ int convrot_peer_barrier(uint32_t* const* flag_arrays, int world, int rank, uint
                          void* stream);
 
 /*
+ * A strided block copy on a copy engine (cudaMemcpy2DAsync, device to
+ * device): rows x width_bytes, pitches in bytes.  dst may be a peer GPU's
+ * memory mapped into this one (symmetric memory).  The tensor-parallel layer
+ * pushes each M-chunk of its column shard into every rank's output with it,
+ * overlapping the next chunk's GEMM; follow the copies with
+ * convrot_peer_barrier.  No reference counterpart.
+ */
+int convrot_copy_2d(void* dst, int64_t dst_pitch, const void* src, int64_t src_pitch, int64_t width_bytes,
+                    int64_t rows, void* stream);
+
+/*
  * The W4A4 linear in one call that allocates nothing: convrot_prepare_i8
  * followed by convrot_w4a4_gemm, with the int8 codes and row scales between
  * them kept in a fixed device array inside the library instead of a buffer

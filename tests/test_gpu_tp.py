@@ -1,10 +1,13 @@
-"""Tensor-parallel W4A4 (column split of N): the gathering GEMM and the flag barrier.
+"""Tensor-parallel W4A4 (column split of N): the gathering GEMM, the peer
+copies and the flag barrier.
 
 On one GPU: the multi-destination epilogue (every destination receives the
-shard's columns at its offset, bit for bit equal to the plain GEMM) and the
-barrier with a world of one.  With two or more GPUs: spawned ranks run
-``ColumnParallelConvRotLinear`` and compare every rank's full output with the
-single-GPU ``ConvRotLinear``, bit for bit.
+shard's columns at its offset, bit for bit equal to the plain GEMM), the
+strided block copy, and the barrier with a world of one and with a peer that
+never arrives.  With two or more GPUs: spawned ranks run
+``ColumnParallelConvRotLinear`` with both gathers (copy-engine in 4 and in 1
+blocks of rows, epilogue peer stores) and compare every rank's full output
+with the single-GPU ``ConvRotLinear``, bit for bit.
 """
 
 from __future__ import annotations
@@ -72,6 +75,21 @@ def test_gather_rejects_bad_arguments():
     assert rc == _lib.ERR_INVALID  # ldc < col_offset + n
 
 
+def test_copy_2d_moves_a_column_block():
+    lib = _lib.load()
+    src = torch.arange(64 * 96, dtype=torch.int16, device=dev()).reshape(64, 96)
+    dst = torch.full((64, 96), -1, dtype=torch.int16, device=dev())
+    # rows 8..40, columns 16..48 (bytes 32..96 of each 192-byte row)
+    _lib.check(lib.convrot_copy_2d(ctypes.c_void_p(dst.data_ptr() + (8 * 96 + 16) * 2), 96 * 2,
+                                   ctypes.c_void_p(src.data_ptr() + (8 * 96 + 16) * 2), 96 * 2, 32 * 2, 32,
+                                   _lib.stream_of(src)), "copy")
+    torch.cuda.synchronize()
+    want = torch.full_like(dst, -1)
+    want[8:40, 16:48] = src[8:40, 16:48]
+    assert torch.equal(dst, want)
+    assert lib.convrot_copy_2d(_lib.ptr(dst), 10, _lib.ptr(src), 10, 20, 1, None) == _lib.ERR_INVALID
+
+
 def test_peer_barrier_world_one():
     flags = torch.zeros(1, dtype=torch.int32, device=dev())
     ptrs = (ctypes.c_void_p * 1)(flags.data_ptr())
@@ -99,16 +117,21 @@ def _tp_rank(rank, world, port, result_path):
                             timeout=datetime.timedelta(seconds=60), device_id=device)
     ok = True
     try:
-        m, k, n = 513, 3072, 64 * 32 * world
+        m, k, n = 1100, 3072, 64 * 32 * world
         layer = _layer(k, n, 7, device)
-        tp = ColumnParallelConvRotLinear.from_full(layer)
-        for step in range(3):
-            g = torch.Generator(device=device).manual_seed(100 + step)
-            x = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
-            want = layer(x)
-            got = tp(x)
+        for gather, chunks in (("copy-engine", 4), ("copy-engine", 1), ("epilogue", 1)):
+            tp = ColumnParallelConvRotLinear.from_full(layer, gather=gather, chunks=chunks)
+            for step in range(3):
+                g = torch.Generator(device=device).manual_seed(100 + step)
+                x = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
+                want = layer(x)
+                got = tp(x)
+                torch.cuda.synchronize()
+                ok &= bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+            tp._out.clear()
+            tp._flags = None
             torch.cuda.synchronize()
-            ok &= bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+            dist.barrier()
         ok &= _lib.take_device_error() == 0
     finally:
         dist.barrier()

@@ -823,13 +823,15 @@ VIDEO_KN = ((5120, 15360), (5120, 13824), (13824, 5120))
 
 def run_video_tp(args, rank, world, local, steps: int, warmup: int):
     """Large video-DiT linears with the weights N-split over the ranks
-    (``ColumnParallelConvRotLinear``): the all-gather of the outputs is fused
-    into the GEMM epilogue (peer stores), then a flag barrier.  One step = the
-    three linears on M = 32760 tokens, timed eagerly (the barrier epoch
-    advances every call) with CUDA events, max over ranks.  Also timed: each
-    rank's GEMMs writing only its own shard (compute only), and the same
-    shard GEMMs followed by an NCCL all_gather_into_tensor and the permute to
-    (M, N) (the library-collective arm).  Parity: every rank compares the
+    (``ColumnParallelConvRotLinear``, its default ``gather="auto"``): the
+    all-gather of the outputs overlaps the GEMM, run in row blocks, by copy
+    engine pushes and (from 8 GPUs) epilogue peer stores, then a flag
+    barrier.  One step = the three linears on M = 32760 tokens, timed
+    eagerly (the barrier epoch advances every call) with CUDA events, max
+    over ranks.  Also timed: the layer's other gathers, each rank's GEMMs
+    writing only its own shard (compute only), and the same shard GEMMs
+    followed by an NCCL all_gather_into_tensor and the permute to (M, N)
+    (the library-collective arm).  Parity: every rank compares the
     gathered output of each linear with the single-GPU ConvRotLinear of the
     full weight, bit for bit."""
 
@@ -923,13 +925,16 @@ def run_video_tp(args, rank, world, local, steps: int, warmup: int):
         ms = timed(step, steps)
     local_ms = timed(local_only, steps)
     nccl_ms = timed(nccl_step, steps) if world > 1 else None
-    epilogue_ms = None
-    if world > 1:  # the other gather: peer stores from the GEMM epilogue
+    arms = {}  # the other gathers of the same layers (peer stores from the epilogue, copy engines, the split)
+    default_epi = layers[0].epilogue_peer_count()
+    if world > 1:
+        for gather in ("epilogue", "copy-engine", "split"):
+            for layer in layers:
+                layer.gather = gather
+            if layers[0].epilogue_peer_count() != default_epi:
+                arms[gather] = round(timed(step, steps), 4)
         for layer in layers:
-            layer.gather = "epilogue"
-        epilogue_ms = timed(step, steps)
-        for layer in layers:
-            layer.gather = "copy-engine"
+            layer.gather = "auto"
     ops = sum(2 * VIDEO_M * k * n for k, n in VIDEO_KN)
     out_bytes = sum(VIDEO_M * n * 2 for k, n in VIDEO_KN)
     recv = out_bytes * (world - 1) // world
@@ -939,12 +944,13 @@ def run_video_tp(args, rank, world, local, steps: int, warmup: int):
         "parity_bit_exact": parity, "compute_only_ms": round(local_ms, 4), "exchange_ms": round(exch, 4),
         "received_bytes_per_rank": recv,
         "exchange_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1) if world > 1 else None,
-        "gather": "copy-engine (4 row blocks, one strided peer copy per block and peer on side streams)",
-        "epilogue_gather_arm_ms": None if epilogue_ms is None else round(epilogue_ms, 4),
+        "gather": (f"auto: 4 row blocks; GEMM epilogue peer stores to {default_epi} peer(s), one strided "
+                   f"copy-engine copy per block to each of the other {max(world - 1 - default_epi, 0)}"),
+        "other_gather_arms_ms": arms,
         "nccl_allgather_arm_ms": None if nccl_ms is None else round(nccl_ms, 4),
         "nccl_allgather_arm_tops": None if nccl_ms is None else round(ops / (nccl_ms * 1e-3) / 1e12, 2),
         "m": VIDEO_M, "kn": [list(p) for p in VIDEO_KN],
-        "parallelism": f"tp{world} (N split; all-gather by copy engines overlapping the chunked GEMM)",
+        "parallelism": f"tp{world} (N split; all-gather overlapping the chunked GEMM)",
         "clocks": clocks.summary(), "device_error": _lib.take_device_error(),
     }
     for layer in layers:
@@ -1002,7 +1008,7 @@ def summarize(line):
     if tp:
         s["video_tp"] = {"n_gpus": tp["n_gpus"], "tops": tp["tops"], "ms": tp["ms_per_step"],
                          "parity": tp["parity_bit_exact"], "compute_ms": tp["compute_only_ms"],
-                         "exchange_ms": tp["exchange_ms"], "epilogue_arm_ms": tp["epilogue_gather_arm_ms"],
+                         "exchange_ms": tp["exchange_ms"], "other_gathers_ms": tp["other_gather_arms_ms"],
                          "nccl_arm_ms": tp["nccl_allgather_arm_ms"]}
     dit = line.get("dit")
     if dit:

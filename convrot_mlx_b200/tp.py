@@ -10,14 +10,20 @@ it (cheaper than broadcasting the codes).  Every rank's full (M, N) output
 buffer is symmetric memory, mapped on every GPU, and the all-gather crosses
 NVLink one of two ways:
 
-* ``gather="copy-engine"`` (the default): the GEMM runs in ``chunks`` blocks
-  of rows into this rank's own buffer; after each block one strided copy per
-  peer (``convrot_copy_2d``) pushes it into the peers' buffers on side
-  streams, so the copy engines carry block i while the SMs compute block
-  i + 1.  Measured on B200 for the video-DiT linears, 4.34 ms per step at 4
-  GPUs and 4.26 ms at 2, against 5.10 / 4.38 ms for the epilogue gather.
+* ``gather="copy-engine"``: the GEMM runs in ``chunks`` blocks of rows into
+  this rank's own buffer; after each block one strided copy per peer
+  (``convrot_copy_2d``) pushes it into the peers' buffers on side streams,
+  so the copy engines carry block i while the SMs compute block i + 1.
 * ``gather="epilogue"``: the GEMM's epilogue (``convrot_w4a4_gemm_gather``)
   stores each output tile into every rank's buffer itself, as peer stores.
+* ``gather="split"``: both at once, for different peers.  The chunked
+  GEMM's epilogue stores into this rank's buffer and those of the next
+  ``epilogue_peers`` ranks; the copy engines push each block to the rest.
+  The two use separate hardware: on B200, with all 8 ranks pushing at once,
+  the copy engines carry ~400 GB/s per GPU and the epilogue's peer stores
+  ~370 GB/s, below the ~770 GB/s a GPU's links take.
+* ``gather="auto"`` (the default): copy engines alone up to 4 ranks (where
+  they carry 650-740 GB/s), the split above that.
 
 Either way a flag barrier (``convrot_peer_barrier``) then makes every rank's
 full output visible.
@@ -49,6 +55,7 @@ from .core import (
 )
 
 _MAX_WORLD = 8
+_GATHERS = ("auto", "copy-engine", "epilogue", "split")
 
 
 def shard_range(out_features: int, world: int, rank: int, layout: int) -> tuple[int, int]:
@@ -86,14 +93,17 @@ class ColumnParallelConvRotLinear(nn.Module):
 
     def __init__(self, in_features: int, out_features: int, *, group: dist.ProcessGroup | None = None,
                  bias: bool = True, group_size: int = CONVROT_GROUP_SIZE, backend: str = "mpp-w4a4",
-                 device=None, gather: str = "copy-engine", chunks: int = 4) -> None:
+                 device=None, gather: str = "auto", chunks: int = 4, epilogue_peers: int | None = None) -> None:
         super().__init__()
-        if gather not in ("copy-engine", "epilogue"):
-            raise ValueError(f"gather must be 'copy-engine' or 'epilogue', got {gather!r}")
+        if gather not in _GATHERS:
+            raise ValueError(f"gather must be one of {_GATHERS}, got {gather!r}")
         if chunks < 1:
             raise ValueError(f"chunks must be positive, got {chunks}")
+        if epilogue_peers is not None and epilogue_peers < 0:
+            raise ValueError(f"epilogue_peers must be non-negative, got {epilogue_peers}")
         self.gather = gather
         self.chunks = chunks
+        self.epilogue_peers = epilogue_peers
         self._side = None  # copy-engine gather: one stream per peer
         self.group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(self.group)
@@ -118,13 +128,13 @@ class ColumnParallelConvRotLinear(nn.Module):
         self._calls = 0     # output buffer = calls % 2
 
     @classmethod
-    def from_full(cls, layer: ConvRotLinear, group: dist.ProcessGroup | None = None, *, gather: str = "copy-engine",
-                  chunks: int = 4) -> "ColumnParallelConvRotLinear":
+    def from_full(cls, layer: ConvRotLinear, group: dist.ProcessGroup | None = None, *, gather: str = "auto",
+                  chunks: int = 4, epilogue_peers: int | None = None) -> "ColumnParallelConvRotLinear":
         """Shard a full (already quantized) ConvRotLinear on every rank."""
 
         tp = cls(layer.in_features, layer.out_features, group=group, bias=layer.source_has_bias,
                  group_size=layer.group_size, backend=layer.backend, device=layer.qweight.device, gather=gather,
-                 chunks=chunks)
+                 chunks=chunks, epilogue_peers=epilogue_peers)
         tp.qweight = shard_weight(layer.qweight, tp.layout, tp.start, tp.stop)
         tp.scales = _f32_vec(layer.scales)[tp.start : tp.stop].clone()
         tp.bias = _f32_vec(layer.bias)[tp.start : tp.stop].clone()
@@ -175,7 +185,8 @@ class ColumnParallelConvRotLinear(nn.Module):
         lib = _lib.load()
         stream = _lib.stream_of(x2d)
         codes, xscales = _prepare(x2d, self.group_size, packed=False)
-        if self.gather == "epilogue" or self.world == 1:
+        epi = self.epilogue_peer_count()
+        if self.world == 1 or (epi == self.world - 1 and self.gather != "split"):
             _lib.check(
                 lib.convrot_w4a4_gemm_gather(
                     _lib.ptr(codes), _lib.ptr(self.qweight), self.layout, _lib.ptr(xscales), _lib.ptr(self.scales),
@@ -185,16 +196,30 @@ class ColumnParallelConvRotLinear(nn.Module):
                 "tensor-parallel W4A4 GEMM",
             )
         else:
-            self._gemm_and_copy(lib, codes, xscales, out, out_ptrs, m, x.dtype, stream)
+            self._gemm_and_copy(lib, codes, xscales, out, out_ptrs, m, x.dtype, stream, epi)
         _lib.check(lib.convrot_peer_barrier(ctypes.cast(flag_ptrs, ctypes.POINTER(ctypes.c_void_p)), self.world,
                                             self.rank, self._epoch, stream), "peer barrier")
         return out.reshape(*lead, self.out_features)
 
-    def _gemm_and_copy(self, lib, codes, xscales, out, out_ptrs, m, dtype, stream) -> None:
-        """The copy-engine gather: the shard GEMM in blocks of rows into this
-        rank's buffer, each block pushed to every peer by a strided copy on a
-        side stream while the next block computes; the current stream then
-        waits for every copy."""
+    def epilogue_peer_count(self) -> int:
+        """How many peers the GEMM's epilogue stores into; the copy engines
+        serve the other ``world - 1 - epilogue_peer_count()``."""
+
+        peers = self.world - 1
+        if self.gather == "epilogue" or peers == 0:
+            return peers
+        if self.gather == "copy-engine":
+            return 0
+        if self.gather == "split":
+            return min(peers, peers // 2 if self.epilogue_peers is None else self.epilogue_peers)
+        return 0 if self.world <= 4 else peers // 2
+
+    def _gemm_and_copy(self, lib, codes, xscales, out, out_ptrs, m, dtype, stream, epi: int) -> None:
+        """The chunked gathers: the shard GEMM in blocks of rows into this
+        rank's buffer and those of the next ``epi`` ranks (epilogue peer
+        stores), each block pushed to the remaining peers by a strided copy
+        on a side stream while the next block computes; the current stream
+        then waits for every copy."""
 
         dev = out.device
         cur = torch.cuda.current_stream(dev)
@@ -206,34 +231,37 @@ class ColumnParallelConvRotLinear(nn.Module):
         rows = -(-m // self.chunks)
         rows = -(-rows // 256) * 256  # whole 256-row pair tiles
         own = out.data_ptr()
+        order = [(self.rank + i) % self.world for i in range(1, self.world)]
+        by_epilogue, by_copy = order[:epi], order[epi:]
+        bases = [own] + [int(out_ptrs[p]) for p in by_epilogue]
         for r0 in range(0, m, rows):
             mr = min(rows, m - r0)
-            dst = (ctypes.c_void_p * 1)(own + r0 * ldc * elt)
+            dst = (ctypes.c_void_p * len(bases))(*[b + r0 * ldc * elt for b in bases])
             _lib.check(
                 lib.convrot_w4a4_gemm_gather(
                     ctypes.c_void_p(codes.data_ptr() + r0 * k), _lib.ptr(self.qweight), self.layout,
-                    ctypes.c_void_p(xscales.data_ptr() + 4 * r0), _lib.ptr(self.scales), _lib.ptr(self.bias), dst, 1,
-                    ldc, self.start, _dtype_code(dtype), mr, self.shard_features, k, stream,
+                    ctypes.c_void_p(xscales.data_ptr() + 4 * r0), _lib.ptr(self.scales), _lib.ptr(self.bias), dst,
+                    len(bases), ldc, self.start, _dtype_code(dtype), mr, self.shard_features, k, stream,
                 ),
                 "tensor-parallel W4A4 GEMM",
             )
+            if not by_copy:
+                continue
             done = torch.cuda.Event()
             done.record(cur)
             offset = (r0 * ldc + self.start) * elt
-            for p in range(self.world):
-                if p == self.rank:
-                    continue
+            for p in by_copy:
                 side = self._side[p]
                 side.wait_event(done)
                 _lib.check(lib.convrot_copy_2d(ctypes.c_void_p(int(out_ptrs[p]) + offset), ldc * elt,
                                                ctypes.c_void_p(own + offset), ldc * elt, self.shard_features * elt,
                                                mr, ctypes.c_void_p(side.cuda_stream)), "peer copy")
-        for p in range(self.world):
-            if p != self.rank:
-                copied = torch.cuda.Event()
-                copied.record(self._side[p])
-                cur.wait_event(copied)
+        for p in by_copy:
+            copied = torch.cuda.Event()
+            copied.record(self._side[p])
+            cur.wait_event(copied)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, world={self.world}, "
-                f"rank={self.rank}, columns=[{self.start}, {self.stop}), gather={self.gather}")
+                f"rank={self.rank}, columns=[{self.start}, {self.stop}), gather={self.gather}, "
+                f"epilogue_peers={self.epilogue_peer_count()}")

@@ -5,9 +5,10 @@ On one GPU: the multi-destination epilogue (every destination receives the
 shard's columns at its offset, bit for bit equal to the plain GEMM), the
 strided block copy, and the barrier with a world of one and with a peer that
 never arrives.  With two or more GPUs: spawned ranks run
-``ColumnParallelConvRotLinear`` with both gathers (copy-engine in 4 and in 1
-blocks of rows, epilogue peer stores) and compare every rank's full output
-with the single-GPU ``ConvRotLinear``, bit for bit.
+``ColumnParallelConvRotLinear`` with every gather (copy engines in 4 and in
+1 blocks of rows, epilogue peer stores, the split of peers between the two,
+the chunked GEMM storing into every peer) and compare every rank's full
+output with the single-GPU ``ConvRotLinear``, bit for bit.
 """
 
 from __future__ import annotations
@@ -119,8 +120,10 @@ def _tp_rank(rank, world, port, result_path):
     try:
         m, k, n = 1100, 3072, 64 * 32 * world
         layer = _layer(k, n, 7, device)
-        for gather, chunks in (("copy-engine", 4), ("copy-engine", 1), ("epilogue", 1)):
-            tp = ColumnParallelConvRotLinear.from_full(layer, gather=gather, chunks=chunks)
+        arms = (("auto", 4, None), ("copy-engine", 4, None), ("copy-engine", 1, None), ("epilogue", 1, None),
+                ("split", 4, None), ("split", 3, world - 1))  # the last: chunked, every peer by epilogue stores
+        for gather, chunks, epi in arms:
+            tp = ColumnParallelConvRotLinear.from_full(layer, gather=gather, chunks=chunks, epilogue_peers=epi)
             for step in range(3):
                 g = torch.Generator(device=device).manual_seed(100 + step)
                 x = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)

@@ -74,3 +74,21 @@ def test_gloo_world_two_gathers_full_weight(tmp_path, layout):
     assert ctx.join(timeout=120) or ctx.join(timeout=30)
     for r in range(2):
         assert open(f"{path}.{r}").read() == "ok"
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_gather_plan_by_world(world):
+    from convrot_mlx_b200.tp import ColumnParallelConvRotLinear
+
+    def plan(gather, epilogue_peers=None):
+        tp = object.__new__(ColumnParallelConvRotLinear)  # the plan reads only these three fields
+        tp.world, tp.gather, tp.epilogue_peers = world, gather, epilogue_peers
+        return tp.epilogue_peer_count()
+
+    peers = world - 1
+    assert plan("epilogue") == peers
+    assert plan("copy-engine") == 0
+    assert plan("split") == peers // 2
+    assert plan("split", 99) == peers
+    assert plan("split", 1) == min(1, peers)
+    assert plan("auto") == (0 if world <= 4 else peers // 2)

@@ -964,7 +964,9 @@ def run_video_tp(args, rank, world, local, steps: int, warmup: int):
 def run_case(args):
     """One kernel on one shape, launched ``--case-launches`` times on the
     default stream (eager), for profilers: ``--case gemm`` runs the W4A4 GEMM
-    (K x packed-N weights), ``--case prep`` the fused rotate + A4 quantize."""
+    (K x packed-N weights; the swap-AB kernel for m <= 8), ``--case prep``
+    the fused rotate + A4 quantize, ``--case modnorm`` the same fused with a
+    modulated LayerNorm."""
 
     import convrot_mlx_b200 as cr
     from convrot_mlx_b200 import _lib
@@ -975,6 +977,14 @@ def run_case(args):
     if args.case == "prep":
         for _ in range(args.case_launches):
             cr.metal_fused_prepare_convrot_activation_i8(x, args.group)
+    elif args.case == "modnorm":
+        from convrot_mlx_b200.core import modulated_norm_prepare_i8
+
+        g = torch.Generator(device=device).manual_seed(SEED + 1)
+        shift, scale = ((torch.randn((1, 1, k), generator=g, device=device) * 0.5).to(torch.bfloat16)
+                        for _ in range(2))
+        for _ in range(args.case_launches):
+            modulated_norm_prepare_i8(x.view(1, m, k), shift, scale, 1e-6, args.group)
     else:
         layer, _, _ = make_linear(k, n, SEED, device)
         codes, xs = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
@@ -1029,7 +1039,7 @@ def main(argv=None):
                          "tensor-parallel and config-4 DiT entries added; flux-sweep: config 3 alone; video-tp: "
                          "config 5 alone; dit: config 4 alone")
     ap.add_argument("--dit-gens", type=int, default=2, help="timed 20-step generations per DiT arm in --workload all")
-    ap.add_argument("--case", choices=("gemm", "prep"), help="run one kernel on one shape (for profilers) and exit")
+    ap.add_argument("--case", choices=("gemm", "prep", "modnorm"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=3072)
     ap.add_argument("--n", type=int, default=12288)

@@ -80,10 +80,13 @@ def test_gloo_world_two_gathers_full_weight(tmp_path, layout):
 def test_gather_plan_by_world(world):
     from convrot_mlx_b200.tp import ColumnParallelConvRotLinear
 
+    def layer(gather, epilogue_peers=None, chunks=None):
+        tp = object.__new__(ColumnParallelConvRotLinear)  # the plan reads only these four fields
+        tp.world, tp.gather, tp.epilogue_peers, tp.chunks = world, gather, epilogue_peers, chunks
+        return tp
+
     def plan(gather, epilogue_peers=None):
-        tp = object.__new__(ColumnParallelConvRotLinear)  # the plan reads only these three fields
-        tp.world, tp.gather, tp.epilogue_peers = world, gather, epilogue_peers
-        return tp.epilogue_peer_count()
+        return layer(gather, epilogue_peers).epilogue_peer_count()
 
     peers = world - 1
     assert plan("epilogue") == peers
@@ -92,3 +95,5 @@ def test_gather_plan_by_world(world):
     assert plan("split", 99) == peers
     assert plan("split", 1) == min(1, peers)
     assert plan("auto") == (0 if world <= 4 else peers // 2)
+    assert layer("auto").row_blocks() == (4 if world <= 4 else 2)
+    assert layer("split", chunks=3).row_blocks() == 3

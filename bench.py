@@ -664,8 +664,9 @@ def run_small_m(args, device):
     a CUDA graph of launches over distinct weights (> L2 in total) replayed
     between CUDA events; achieved GB/s = (packed weights + activation codes
     + output) / time against MEASURED_PEAKS.json hbm_gbs.  Beside it the same
-    GEMM forced onto the CTA-pair kernel, and dense bf16 (cuBLAS) on the
-    same shape."""
+    GEMM forced onto the register-fragment GEMV kernel (m <= 8), the
+    swap-AB tcgen05 kernel and the CTA-pair kernel, and dense bf16 (cuBLAS)
+    on the same shape."""
 
     from convrot_mlx_b200 import _lib
 
@@ -695,6 +696,10 @@ def run_small_m(args, device):
         pair_us = graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3
         _lib.check(lib.convrot_set_gemm_route(3), "route")
         swap_us = graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3
+        gemv_us = None
+        if m <= 8:
+            _lib.check(lib.convrot_set_gemm_route(4), "route")
+            gemv_us = round(graph_ms(launches, max(3, args.steps), stream) / n_w * 1e3, 2)
         _lib.check(lib.convrot_set_gemm_route(0), "route")
         dw = [torch.randn((n, k), generator=g, device=device).to(torch.bfloat16) for _ in range(max(2, n_w // 4))]
         xd = torch.randn((m, k), generator=g, device=device).to(torch.bfloat16)
@@ -710,14 +715,15 @@ def run_small_m(args, device):
         gbs = algo / (us * 1e-6) / 1e9
         out.append({"m": m, "k": k, "n": n, "us": round(us, 2), "gbs": round(gbs, 1),
                     "frac": round(gbs / peaks["hbm_gbs"], 4), "kernel": "swap-AB" if m <= 8 else "pair",
-                    "swap_ab_kernel_us": round(swap_us, 2), "pair_kernel_us": round(pair_us, 2),
+                    "gemv_kernel_us": gemv_us, "swap_ab_kernel_us": round(swap_us, 2),
+                    "pair_kernel_us": round(pair_us, 2),
                     "dense_bf16_us": round(dense_us, 2), "speedup_vs_dense_bf16": round(dense_us / us, 2)})
         del qs, dw
     return {"kernel": "default routing: small_m_kernel (swap-AB tcgen05 kind::i8, K split over a cluster, DSMEM "
                       "reduction) for m <= 8, else pair_gemm_kernel",
             "bound": "hbm", "peak_gbs": peaks["hbm_gbs"],
             "bytes_note": "packed weights K N / 2 + codes M K + bf16 output 2 M N + scales/bias 8 N + 4 M per launch",
-            "shapes": out}
+            "shapes": out, "device_error": _lib.take_device_error()}
 
 
 # ---------------------------------------------------------------------------
@@ -1034,10 +1040,10 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", choices=("all", "flux-sweep", "video-tp", "dit"), default="all",
+    ap.add_argument("--workload", choices=("all", "flux-sweep", "video-tp", "dit", "small-m"), default="all",
                     help="all (default): the config-3 FLUX sweep line with the config-2 prep, config-5 "
                          "tensor-parallel and config-4 DiT entries added; flux-sweep: config 3 alone; video-tp: "
-                         "config 5 alone; dit: config 4 alone")
+                         "config 5 alone; dit: config 4 alone; small-m: the m <= 64 GEMM entry alone")
     ap.add_argument("--dit-gens", type=int, default=2, help="timed 20-step generations per DiT arm in --workload all")
     ap.add_argument("--case", choices=("gemm", "prep", "modnorm"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
@@ -1066,6 +1072,8 @@ def main(argv=None):
             rc = 0 if line["parity_bit_exact"] else 1
         elif args.workload == "dit":
             line = run_dit(args, rank, world, local, args.steps, args.warmup)
+        elif args.workload == "small-m":
+            line = run_small_m(args, device)
         else:
             line = run_ours(args, rank, world, local)
             if args.workload == "all":

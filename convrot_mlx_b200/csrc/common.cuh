@@ -57,6 +57,13 @@ int small_m_auto_rows();
 int launch_small_m(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales, const float* wscales,
                    const float* bias, void* out, int out_dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream);
 
+// Register-fragment W4A4 GEMV for at most 8 activation rows (gemv_w4a4.cu):
+// the shapes it takes, and its launch after convrot_w4a4_gemm's argument
+// checks.
+bool gemv_supported(int layout, int64_t m, int64_t n, int64_t k);
+int launch_gemv(const int8_t* act, const uint8_t* qweight, int layout, const float* xscales, const float* wscales,
+                const float* bias, void* out, int out_dtype, int64_t m, int64_t n, int64_t k, cudaStream_t stream);
+
 namespace w4a4 {
 // Argument checks of convrot_w4a4_gemm (gemm_w4a4.cu); need_act false skips
 // the activation and row-scale pointers (for callers that produce them).

@@ -1227,8 +1227,9 @@ static int launch(const CUtensorMap& map, const Params& p, cudaStream_t stream) 
 
 // Kernel routing of convrot_w4a4_gemm: 0 automatic, 1 every shape to the
 // one-CTA kernel, 2 every shape the CTA-pair kernel takes to it, 3 every
-// shape the swap-AB kernel takes (m <= 64) to it (set by
-// convrot_set_gemm_route, for tests and A/B measurements).
+// shape the swap-AB kernel takes (m <= 64) to it, 4 every shape the GEMV
+// kernel takes (m <= 8) to it (set by convrot_set_gemm_route, for tests and
+// A/B measurements).
 std::atomic<int> g_gemm_route{0};
 
 int forced_kernel() { return g_gemm_route.load(std::memory_order_relaxed); }
@@ -1288,6 +1289,8 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
   p.layout = layout;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int forced = w4a4::forced_kernel();
+  if (forced == 4 && gemv_supported(layout, m, n, k))
+    return launch_gemv(act, qweight, layout, xscales, wscales, bias, out, out_dtype, m, n, k, s);
   if (((forced == 0 && m <= small_m_auto_rows()) || forced == 3) && small_m_supported(layout, m, n, k))
     return launch_small_m(act, qweight, layout, xscales, wscales, bias, out, out_dtype, m, n, k, s);
   const bool use_pair = w4a4::pair_supported(layout, n, k) && forced != 1;
@@ -1430,7 +1433,7 @@ int convrot_w4a16_gemm(const void* act, int act_dtype, const uint8_t* qweight, i
 
 int convrot_set_gemm_route(int route) {
   using namespace convrot;
-  CONVROT_REQUIRE(route >= 0 && route <= 3, CONVROT_ERR_INVALID, "GEMM route must be 0-3, got %d", route);
+  CONVROT_REQUIRE(route >= 0 && route <= 4, CONVROT_ERR_INVALID, "GEMM route must be 0-4, got %d", route);
   w4a4::g_gemm_route.store(route, std::memory_order_relaxed);
   return CONVROT_OK;
 }

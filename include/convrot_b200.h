@@ -256,9 +256,11 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
  * 0), else the CTA-pair kernel where it applies (k % 128 == 0; K x packed-N
  * with n % 32 == 0), else the one-CTA kernel; route 1: the one-CTA kernel
  * for every shape; route 2: the CTA-pair kernel wherever it applies (never
- * the swap-AB one); route 3: the swap-AB kernel wherever it applies (m <=
- * 64).  All give the same bits.  Process-wide; for tests and A/B timing.
- * No reference counterpart.
+ * a small-m one); route 3: the swap-AB kernel wherever it applies (m <=
+ * 64); route 4: the register-fragment GEMV kernel wherever it applies
+ * (m <= 8; K x packed-N with n % 16 == 0, or N x packed-K).  All give the
+ * same bits.  Process-wide; for tests and A/B timing.  No reference
+ * counterpart.
  */
 int convrot_set_gemm_route(int route);
 

@@ -714,12 +714,13 @@ def run_small_m(args, device):
         algo = w_bytes + m * k + 2 * m * n + 8 * n + 4 * m
         gbs = algo / (us * 1e-6) / 1e9
         out.append({"m": m, "k": k, "n": n, "us": round(us, 2), "gbs": round(gbs, 1),
-                    "frac": round(gbs / peaks["hbm_gbs"], 4), "kernel": "swap-AB" if m <= 8 else "pair",
+                    "frac": round(gbs / peaks["hbm_gbs"], 4), "kernel": "gemv" if m <= 8 else "pair",
                     "gemv_kernel_us": gemv_us, "swap_ab_kernel_us": round(swap_us, 2),
                     "pair_kernel_us": round(pair_us, 2),
                     "dense_bf16_us": round(dense_us, 2), "speedup_vs_dense_bf16": round(dense_us / us, 2)})
         del qs, dw
-    return {"kernel": "default routing: small_m_kernel (swap-AB tcgen05 kind::i8, K split over a cluster, DSMEM "
+    return {"kernel": "default routing: gemv_kernel (per-warp cp.async rings of packed weights, byte-permuted "
+                      "into mma.sync m16n8k32 s8 register fragments, K split over warps and a cluster, DSMEM "
                       "reduction) for m <= 8, else pair_gemm_kernel",
             "bound": "hbm", "peak_gbs": peaks["hbm_gbs"],
             "bytes_note": "packed weights K N / 2 + codes M K + bf16 output 2 M N + scales/bias 8 N + 4 M per launch",
@@ -996,6 +997,7 @@ def run_case(args):
         codes, xs = cr.metal_fused_prepare_convrot_activation_i8(x, GROUP)
         out = torch.empty((m, n), dtype=torch.bfloat16, device=device)
         lib = _lib.load()
+        _lib.check(lib.convrot_set_gemm_route(args.route), "route")
         for _ in range(args.case_launches):
             _lib.check(lib.convrot_w4a4_gemm(_lib.ptr(codes), _lib.ptr(layer.qweight), _lib.LAYOUT_KN, _lib.ptr(xs),
                                              _lib.ptr(layer.scales), _lib.ptr(layer.bias), _lib.ptr(out), _lib.BF16,
@@ -1051,6 +1053,8 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=12288)
     ap.add_argument("--group", type=int, default=GROUP)
     ap.add_argument("--case-launches", type=int, default=3)
+    ap.add_argument("--route", type=int, default=0, help="--case gemm: convrot_set_gemm_route (0 automatic, "
+                    "1 one-CTA, 2 CTA-pair, 3 swap-AB, 4 GEMV)")
     args = ap.parse_args(argv)
     if args.case:
         return run_case(args)

@@ -388,10 +388,12 @@ bool small_m_supported(int layout, int64_t m, int64_t n, int64_t k) {
   return m >= 1 && m <= small_m::kMaxRows && k % 128 == 0 && (layout == CONVROT_LAYOUT_NK || n % 32 == 0);
 }
 
-// Rows up to which the default routing prefers this kernel: measured on
-// B200, it matches or beats the CTA-pair kernel at m <= 8 (both are bound by
-// per-stage hand-off latency there, and its K split fills more SMs), while
-// from m = 16 the CTA-pair kernel is faster.
+// Rows up to which the default routing prefers this kernel to the CTA-pair
+// one: measured on B200, it matches or beats the CTA-pair kernel at m <= 8
+// (both are bound by per-stage hand-off latency there, and its K split fills
+// more SMs), while from m = 16 the CTA-pair kernel is faster.  The default
+// routing tries the GEMV kernel (gemv_w4a4.cu, 1.5-2.2x faster at m <= 8)
+// before either, so this one serves route 3 and shapes the GEMV declines.
 int small_m_auto_rows() { return 8; }
 
 template <int LAYOUT, typename TOut>

@@ -1289,7 +1289,7 @@ int convrot_w4a4_gemm(const int8_t* act, const uint8_t* qweight, int layout, con
   p.layout = layout;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int forced = w4a4::forced_kernel();
-  if (forced == 4 && gemv_supported(layout, m, n, k))
+  if ((forced == 0 || forced == 4) && gemv_supported(layout, m, n, k))
     return launch_gemv(act, qweight, layout, xscales, wscales, bias, out, out_dtype, m, n, k, s);
   if (((forced == 0 && m <= small_m_auto_rows()) || forced == 3) && small_m_supported(layout, m, n, k))
     return launch_small_m(act, qweight, layout, xscales, wscales, bias, out, out_dtype, m, n, k, s);

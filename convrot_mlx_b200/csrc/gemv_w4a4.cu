@@ -7,9 +7,11 @@
 // is reading the K * N / 2 packed weight bytes from HBM once.  A tile kernel
 // stages weights through shared memory and TMEM, and each of its stages waits
 // on the previous hand-off; at m <= 8 those waits, not bandwidth, set its
-// time.  Here every thread loads its weight bytes with plain 8- or 16-byte
-// global loads into registers, turns them into int8 MMA fragments with byte
-// permutes, and issues register-operand MMAs
+// time.  Here each warp streams its share of the weights through a small
+// ring of its own in shared memory, filled by cp.async copies that its lanes
+// issue several K units ahead (no barrier with any other warp), reads them
+// into registers, turns them into int8 MMA fragments with byte permutes, and
+// issues register-operand MMAs
 //
 //   C[n, r] (int32) += W16[n, k] x A[r, k]^T,
 //   mma.sync.m16n8k32.row.col.s32.s8.s8.s32,
@@ -22,14 +24,14 @@
 // Fragment construction.  The MMA only requires that the threads agree on
 // which real column each fragment row is and which real k each fragment k
 // index is, so both are chosen to match what a thread loads:
-// * K x packed-N weights: thread (g = lane / 4, t = lane % 4) loads rows
+// * K x packed-N weights: thread (g = lane / 4, t = lane % 4) reads rows
 //   k0 + 8t .. + 7, 16 columns each (8 bytes).  A 4 x 4 byte transpose of
 //   four rows (8 byte permutes) gives words of 4 consecutive k for one byte
 //   position, i.e. for a column pair; shift / mask split the pair.  MMA j of
 //   an 8-column chunk takes columns 2j (fragment row g) and 2j + 1 (row
 //   g + 8); fragment k index 4t + i is real k k0 + 8t + i, and 16 + 4t + i
 //   is k0 + 8t + 4 + i, so the activation fragment is the 8 bytes of row g
-//   at k0 + 8t, one load.
+//   at k0 + 8t, one read.
 // * N x packed-K weights: a 32-bit word of a weight row is 8 consecutive k
 //   of one column; the low nibbles (even k) and high nibbles (odd k) are the
 //   two fragment k halves, and the activation bytes are permuted to match.
@@ -86,23 +88,87 @@ __device__ __forceinline__ void k_range(int units, int rank, int ranks, int warp
   hi = c0 + static_cast<int>(static_cast<int64_t>(c1 - c0) * (warp + 1) / kWarps);
 }
 
+// ---- each warp's ring of K units in shared memory ----------------------------
+// A warp keeps DEPTH - 1 units of its K slice in flight as cp.async copies
+// (issued by its own lanes, no registers held) while it computes on the
+// oldest; bytes in flight are bounded by shared memory, not registers.
+
+// `BYTES` (8 or 16) global -> shared; only `src_bytes` are read, the rest of
+// the destination is zero-filled (0 reads nothing)
+template <int BYTES>
+__device__ __forceinline__ void cp_async(uint32_t dst, const void* src, uint32_t src_bytes) {
+  if constexpr (BYTES == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+
 // ---- K x packed-N weights ----------------------------------------------------
-// One unit = 32 k.  A thread holds rows k0 + 8t + i (i < 8) of its group's 16
-// columns: x[i].x = columns 0-7, x[i].y = 8-15 (byte b = columns 2b, 2b + 1).
+// One unit = 32 k: rows k0 .. k0 + 31 of the CTA's 128 columns (64 bytes a
+// row) and the activation rows' 32 k, in the ring.  Thread (g, t) computes on rows
+// k0 + 8t + i (i < 8), 16 columns each: x[i].x = columns 0-7 of its group,
+// x[i].y = 8-15 (byte b = columns 2b, 2b + 1).
+
+constexpr int kKnW = 32 * 64;           // weight bytes of a unit
+constexpr int kKnSlot = kKnW + 8 * 32;  // + 8 activation rows x 32 k
+constexpr int kKnDepth = 3;
 
 struct KnStep {
   uint2 x[8];
   uint2 a;  // activation row g, k0 + 8t .. + 7
 };
 
-__device__ __forceinline__ void kn_load(KnStep& s, const Params& p, int unit, int col, bool col_ok, int g, int t) {
-  const int k = unit * 32 + 8 * t;
+// Row r of the unit sits at slot row (r % 8) * 4 + r / 8, so the 32 lanes'
+// reads of one i (rows 8t + i) are 256 contiguous bytes.  CHUNK: 16 when the
+// weight rows are 16-byte aligned (N % 32 == 0), else 8.
+// A copy instruction covers whole 64-byte row segments (64 / CHUNK lanes a
+// row), so it touches few cache lines.
+template <int CHUNK>
+__device__ __forceinline__ void kn_issue(uint32_t slot, const Params& p, int unit, int n0, int lane) {
+  constexpr int kLanesPerRow = 64 / CHUNK, kRowsPerCopy = 32 / kLanesPerRow;
   const size_t row_bytes = static_cast<size_t>(p.N) / 2;
-  const uint8_t* w = p.qweight + static_cast<size_t>(k) * row_bytes + col / 2;
+  const int q = lane % kLanesPerRow;  // this lane's chunk of each row segment
+  const int left = (p.N - n0) / 2 - q * CHUNK;  // bytes of the chunk inside the row
+  const uint32_t n = left >= CHUNK ? CHUNK : (left > 0 ? static_cast<uint32_t>(left) : 0u);
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    s.x[i] = col_ok ? __ldg(reinterpret_cast<const uint2*>(w + i * row_bytes)) : make_uint2(0u, 0u);
-  s.a = g < p.M ? __ldg(reinterpret_cast<const uint2*>(p.act + static_cast<size_t>(g) * p.K + k)) : make_uint2(0u, 0u);
+  for (int c = 0; c < 32 / kRowsPerCopy; ++c) {
+    const int r = c * kRowsPerCopy + lane / kLanesPerRow;
+    const uint8_t* src = p.qweight + static_cast<size_t>(unit * 32 + r) * row_bytes + n0 / 2 + q * CHUNK;
+    cp_async<CHUNK>(slot + ((r & 7) * 4 + (r >> 3)) * 64 + q * CHUNK, n ? static_cast<const void*>(src) : p.qweight,
+                    n);
+  }
+}
+
+// the unit's activation rows (zero past M): lanes 0-15, 16 bytes each
+__device__ __forceinline__ void kn_issue_act(uint32_t slot, const Params& p, int unit, int lane) {
+  if (lane < 16) {
+    const int r = lane >> 1, h = lane & 1;
+    const bool ok = r < p.M;
+    cp_async<16>(slot + kKnW + r * 32 + h * 16,
+                 ok ? static_cast<const void*>(p.act + static_cast<size_t>(r) * p.K + unit * 32 + h * 16) : p.act,
+                 ok ? 16u : 0u);
+  }
+}
+
+__device__ __forceinline__ void kn_read(KnStep& s, uint32_t slot, int g, int t) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s.x[i] = lds64(slot + (i * 4 + t) * 64 + 8 * g);
+  s.a = lds64(slot + kKnW + g * 32 + 8 * t);
 }
 
 // 4 x 4 byte transpose: out[b] = byte b of w0..w3 (w0's in the low byte)
@@ -131,33 +197,55 @@ __device__ __forceinline__ void kn_mma(const KnStep& s, int32_t (&acc)[2][4][4])
 }
 
 // ---- N x packed-K weights ----------------------------------------------------
-// One unit = 128 k.  A thread holds, for MMA j, 32 k (16 bytes) at k0 + 32t of
-// columns 16j + g and 16j + g + 8.
+// One unit = 128 k: 64 bytes of each of the CTA's 64 columns and the
+// activation rows' 128 k, in the ring.  Thread (g, t) computes, for MMA j, on 32 k (16
+// bytes) at k0 + 32t of columns 16j + g and 16j + g + 8.
+
+constexpr int kNkW = 64 * 64;
+constexpr int kNkActStride = 144;  // 128 k + 16 bytes, so rows g and g + 1 fall on other banks
+constexpr int kNkSlot = kNkW + 8 * kNkActStride;
+constexpr int kNkDepth = 3;
 
 struct NkStep {
   uint4 wa[4], wb[4];
   uint4 a0, a1;  // activation row g, k0 + 32t .. + 31
 };
 
-__device__ __forceinline__ void nk_load(NkStep& s, const Params& p, int unit, int n0, int g, int t) {
-  const int k = unit * 128 + 32 * t;
-  const bool k_ok = k < p.K;  // K % 32 == 0: a thread's 32 k are all in or all out
+__device__ __forceinline__ void nk_issue(uint32_t slot, const Params& p, int unit, int n0, int lane) {
   const size_t row_bytes = static_cast<size_t>(p.K) / 2;
+  const int kb = unit * 64;                               // the unit's byte offset in a weight row
+  const int kvalid = static_cast<int>(row_bytes) - kb;    // > 0, a multiple of 16
+  const int q = lane & 3;  // this lane's 16 bytes of each column's 64 (4 lanes a column, 8 columns a copy)
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int col = c * 8 + (lane >> 2);
+    const bool ok = n0 + col < p.N && q * 16 < kvalid;
+    const uint8_t* src = p.qweight + static_cast<size_t>(n0 + col) * row_bytes + kb + q * 16;
+    cp_async<16>(slot + col * 64 + q * 16, ok ? static_cast<const void*>(src) : p.qweight, ok ? 16u : 0u);
+  }
+}
+
+// the unit's activation rows (zero past M or K): 64 chunks of 16 bytes
+__device__ __forceinline__ void nk_issue_act(uint32_t slot, const Params& p, int unit, int lane) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int id = lane + 32 * h, r = id >> 3, part = id & 7;
+    const bool ok = r < p.M && unit * 128 + part * 16 < p.K;
+    cp_async<16>(slot + kNkW + r * kNkActStride + part * 16,
+                 ok ? static_cast<const void*>(p.act + static_cast<size_t>(r) * p.K + unit * 128 + part * 16)
+                    : p.act,
+                 ok ? 16u : 0u);
+  }
+}
+
+__device__ __forceinline__ void nk_read(NkStep& s, uint32_t slot, int g, int t) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const int ca = n0 + 16 * j + g, cb = ca + 8;
-    s.wa[j] = (k_ok && ca < p.N) ? __ldg(reinterpret_cast<const uint4*>(p.qweight + ca * row_bytes + k / 2))
-                                 : make_uint4(0u, 0u, 0u, 0u);
-    s.wb[j] = (k_ok && cb < p.N) ? __ldg(reinterpret_cast<const uint4*>(p.qweight + cb * row_bytes + k / 2))
-                                 : make_uint4(0u, 0u, 0u, 0u);
+    s.wa[j] = lds128(slot + (16 * j + g) * 64 + 16 * t);
+    s.wb[j] = lds128(slot + (16 * j + g + 8) * 64 + 16 * t);
   }
-  if (k_ok && g < p.M) {
-    const uint4* a = reinterpret_cast<const uint4*>(p.act + static_cast<size_t>(g) * p.K + k);
-    s.a0 = __ldg(a);
-    s.a1 = __ldg(a + 1);
-  } else {
-    s.a0 = s.a1 = make_uint4(0u, 0u, 0u, 0u);
-  }
+  s.a0 = lds128(slot + kNkW + g * kNkActStride + 32 * t);
+  s.a1 = lds128(slot + kNkW + g * kNkActStride + 32 * t + 16);
 }
 
 __device__ __forceinline__ uint32_t word(const uint4& v, int i) {
@@ -180,35 +268,84 @@ __device__ __forceinline__ void nk_mma(const NkStep& s, int32_t (&acc)[4][4]) {
 
 // ---- the kernel ----------------------------------------------------------------
 
-template <int LAYOUT, typename TOut>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
-  constexpr int CB = LAYOUT == CONVROT_LAYOUT_KN ? kCbKN : kCbNK;
-  __shared__ __align__(16) int32_t red[kWarps][kMaxRows * CB];  // per-warp partial sums [row][column]
+template <int LAYOUT>
+__host__ __device__ constexpr int ring_bytes() {
+  return LAYOUT == CONVROT_LAYOUT_KN ? kWarps * kKnDepth * kKnSlot : kWarps * kNkDepth * kNkSlot;
+}
+
+template <int LAYOUT, int CHUNK, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
+  constexpr bool kKN = LAYOUT == CONVROT_LAYOUT_KN;
+  constexpr int CB = kKN ? kCbKN : kCbNK;
+  constexpr int SLOT = kKN ? kKnSlot : kNkSlot;
+  constexpr int DEPTH = kKN ? kKnDepth : kNkDepth;
+  static_assert(kWarps * kMaxRows * CB * 4 <= ring_bytes<LAYOUT>(), "partial sums overlay the rings");
+  // the warps' rings; after the K loop the same memory holds the per-warp
+  // partial sums red[warp][row * CB + column]
+  extern __shared__ __align__(128) uint8_t smem[];
+  int32_t* red = reinterpret_cast<int32_t*>(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int rank = p.cluster > 1 ? static_cast<int>(cluster_ctarank()) : 0;
   const int n0 = static_cast<int>(blockIdx.x) / p.cluster * CB;
+  const uint32_t ring = smem_u32(smem) + static_cast<uint32_t>(warp * DEPTH * SLOT);
 
+  int lo, hi;
+  k_range(kKN ? p.K / 32 : (p.K + 127) / 128, rank, p.cluster, warp, lo, hi);
+  const int units = hi - lo;
+  auto issue_w = [&](int i) {
+    if constexpr (kKN) kn_issue<CHUNK>(ring + (i % DEPTH) * SLOT, p, lo + i, n0, lane);
+    else nk_issue(ring + (i % DEPTH) * SLOT, p, lo + i, n0, lane);
+  };
+  auto issue_a = [&](int i) {
+    if constexpr (kKN) kn_issue_act(ring + (i % DEPTH) * SLOT, p, lo + i, lane);
+    else nk_issue_act(ring + (i % DEPTH) * SLOT, p, lo + i, lane);
+  };
+  // The packed weights do not come from the previous kernel of the stream
+  // (no kernel of this library that lets its dependents start early writes
+  // packed weights), so the first units' weight copies start before waiting
+  // for it; their activation rows follow after the wait, as one more group.
+  // Commit groups: W0 .. W(D-2), A(0 .. D-2), then one per later unit.
+#pragma unroll
+  for (int i = 0; i < DEPTH - 1; ++i) {
+    if (i < units) issue_w(i);
+    cp_async_commit();
+  }
   grid_dependency_wait();  // the activation codes may come from the previous kernel of the stream
   grid_dependents_launch();
+#pragma unroll
+  for (int i = 0; i < DEPTH - 1; ++i)
+    if (i < units) issue_a(i);
+  cp_async_commit();
 
-  int32_t* mine = red[warp];
-  if constexpr (LAYOUT == CONVROT_LAYOUT_KN) {
-    int32_t acc[2][4][4] = {};
-    const int col = n0 + 16 * g;
-    const bool col_ok = col < p.N;  // N % 16 == 0: a group's 16 columns are all in or all out
-    int lo, hi;
-    k_range(p.K / 32, rank, p.cluster, warp, lo, hi);
-    KnStep s0, s1;
-    if (lo < hi) kn_load(s0, p, lo, col, col_ok, g, t);
-    int u = lo;
-    // two steps of loads in flight: step u + 1 is loaded while step u computes
-    for (; u + 1 < hi; u += 2) {
-      kn_load(s1, p, u + 1, col, col_ok, g, t);
-      kn_mma(s0, acc);
-      if (u + 2 < hi) kn_load(s0, p, u + 2, col, col_ok, g, t);
-      kn_mma(s1, acc);
+  int32_t* mine = red + warp * kMaxRows * CB;
+  // unit i and its activations have landed (this lane's copies): all but
+  // the min(i + 1, DEPTH - 1) most recent groups are complete
+  auto wait_unit = [&](int i) {
+    static_assert(DEPTH >= 2 && DEPTH <= 4, "wait_unit covers rings of 2-4 units");
+    if (DEPTH >= 3 && i == 0) cp_async_wait<1>();
+    else if (DEPTH >= 4 && i == 1) cp_async_wait<2>();
+    else cp_async_wait<DEPTH - 1>();
+  };
+  auto refill = [&](int i) {
+    if (i + DEPTH - 1 < units) {
+      issue_w(i + DEPTH - 1);
+      issue_a(i + DEPTH - 1);
     }
-    if (u < hi) kn_mma(s0, acc);
+    cp_async_commit();
+  };
+  if constexpr (kKN) {
+    int32_t acc[2][4][4] = {};
+    for (int i = 0; i < units; ++i) {
+      refill(i);
+      wait_unit(i);
+      __syncwarp();  // ... and every lane's
+      KnStep s;
+      kn_read(s, ring + (i % DEPTH) * SLOT, g, t);
+      kn_mma(s, acc);
+      __syncwarp();  // all reads of the slot done before it is refilled
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // every warp is out of its ring before the partial sums overlay it
 #pragma unroll
     for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -221,18 +358,17 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
       }
   } else {
     int32_t acc[4][4] = {};
-    int lo, hi;
-    k_range((p.K + 127) / 128, rank, p.cluster, warp, lo, hi);
-    NkStep s0, s1;
-    if (lo < hi) nk_load(s0, p, lo, n0, g, t);
-    int u = lo;
-    for (; u + 1 < hi; u += 2) {
-      nk_load(s1, p, u + 1, n0, g, t);
-      nk_mma(s0, acc);
-      if (u + 2 < hi) nk_load(s0, p, u + 2, n0, g, t);
-      nk_mma(s1, acc);
+    for (int i = 0; i < units; ++i) {
+      refill(i);
+      wait_unit(i);
+      __syncwarp();
+      NkStep s;
+      nk_read(s, ring + (i % DEPTH) * SLOT, g, t);
+      nk_mma(s, acc);
+      __syncwarp();
     }
-    if (u < hi) nk_mma(s0, acc);
+    cp_async_wait<0>();
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int cl = 16 * j + g;
@@ -244,13 +380,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
   }
   __syncthreads();
 
-  // this CTA's partial of rows < M: the sum over its warps, into red[0]
+  // this CTA's partial of rows < M: the sum over its warps, into warp 0's slice
   const int items = p.M * CB;
   for (int i = threadIdx.x; i < items; i += kThreads) {
-    int32_t v = red[0][i];
+    int32_t v = red[i];
 #pragma unroll
-    for (int w = 1; w < kWarps; ++w) v += red[w][i];
-    red[0][i] = v;
+    for (int w = 1; w < kWarps; ++w) v += red[w * kMaxRows * CB + i];
+    red[i] = v;
   }
   if (p.cluster > 1) cluster_sync();
   else __syncthreads();
@@ -259,11 +395,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
     TOut* out = static_cast<TOut*>(p.out);
     for (int i = threadIdx.x; i < items; i += kThreads) {
       const int r = i / CB, n = n0 + i % CB;
-      uint32_t v = static_cast<uint32_t>(red[0][i]);
+      uint32_t v = static_cast<uint32_t>(red[i]);
       uint32_t rem[kMaxCluster];
 #pragma unroll
       for (int q = 1; q < kMaxCluster; ++q)
-        rem[q] = q < p.cluster ? dsmem_ld(mapa_shared(&red[0][i], static_cast<uint32_t>(q))) : 0u;
+        rem[q] = q < p.cluster ? dsmem_ld(mapa_shared(&red[i], static_cast<uint32_t>(q))) : 0u;
 #pragma unroll
       for (int q = 1; q < kMaxCluster; ++q) v += rem[q];
       if (n < p.N) {
@@ -278,12 +414,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const Params p) {
   if (p.cluster > 1) cluster_sync();
 }
 
-template <int LAYOUT, typename TOut>
+template <int LAYOUT, int CHUNK, typename TOut>
 static int launch_t(const Params& p, int col_blocks, cudaStream_t stream) {
+  auto kernel = gemv_kernel<LAYOUT, CHUNK, TOut>;
+  constexpr int smem = ring_bytes<LAYOUT>();
+  CONVROT_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(col_blocks * p.cluster), 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -294,7 +433,7 @@ static int launch_t(const Params& p, int col_blocks, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemv_kernel<LAYOUT, TOut>, p));
+  CONVROT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kernel, p));
   return check_launch("w4a4 gemv");
 }
 
@@ -324,23 +463,31 @@ int launch_gemv(const int8_t* act, const uint8_t* qweight, int layout, const flo
   const int unit = layout == CONVROT_LAYOUT_KN ? 32 : 128;
   const int units = static_cast<int>((k + unit - 1) / unit);
   const int col_blocks = static_cast<int>((n + cb - 1) / cb);
-  // split K over a cluster so that about two CTAs run per SM, with at least
+  // split K over a cluster so that the CTAs make one wave, one per SM (a
+  // second wave, or two CTAs per SM, measured slower on B200), with at least
   // one K unit per warp
-  int c = 2 * device_sm_count() / col_blocks;
+  int c = device_sm_count() / col_blocks;
   if (c > kMaxCluster) c = kMaxCluster;
   if (c > units / kWarps) c = units / kWarps;
   p.cluster = c < 1 ? 1 : c;
   if (layout == CONVROT_LAYOUT_NK) {
     switch (out_dtype) {
-      case CONVROT_BF16: return launch_t<CONVROT_LAYOUT_NK, __nv_bfloat16>(p, col_blocks, stream);
-      case CONVROT_F16: return launch_t<CONVROT_LAYOUT_NK, __half>(p, col_blocks, stream);
-      default: return launch_t<CONVROT_LAYOUT_NK, float>(p, col_blocks, stream);
+      case CONVROT_BF16: return launch_t<CONVROT_LAYOUT_NK, 16, __nv_bfloat16>(p, col_blocks, stream);
+      case CONVROT_F16: return launch_t<CONVROT_LAYOUT_NK, 16, __half>(p, col_blocks, stream);
+      default: return launch_t<CONVROT_LAYOUT_NK, 16, float>(p, col_blocks, stream);
+    }
+  }
+  if (n % 32 == 0) {  // weight rows 16-byte aligned
+    switch (out_dtype) {
+      case CONVROT_BF16: return launch_t<CONVROT_LAYOUT_KN, 16, __nv_bfloat16>(p, col_blocks, stream);
+      case CONVROT_F16: return launch_t<CONVROT_LAYOUT_KN, 16, __half>(p, col_blocks, stream);
+      default: return launch_t<CONVROT_LAYOUT_KN, 16, float>(p, col_blocks, stream);
     }
   }
   switch (out_dtype) {
-    case CONVROT_BF16: return launch_t<CONVROT_LAYOUT_KN, __nv_bfloat16>(p, col_blocks, stream);
-    case CONVROT_F16: return launch_t<CONVROT_LAYOUT_KN, __half>(p, col_blocks, stream);
-    default: return launch_t<CONVROT_LAYOUT_KN, float>(p, col_blocks, stream);
+    case CONVROT_BF16: return launch_t<CONVROT_LAYOUT_KN, 8, __nv_bfloat16>(p, col_blocks, stream);
+    case CONVROT_F16: return launch_t<CONVROT_LAYOUT_KN, 8, __half>(p, col_blocks, stream);
+    default: return launch_t<CONVROT_LAYOUT_KN, 8, float>(p, col_blocks, stream);
   }
 }
 

@@ -252,9 +252,11 @@ int convrot_w4a4_linear_static(const void* x, int x_dtype, int group_size,
 
 /*
  * Diagnostics: which kernel convrot_w4a4_gemm runs.  route 0 (the default):
- * the swap-AB kernel for m <= 8 (k % 128 == 0; K x packed-N with n % 32 ==
- * 0), else the CTA-pair kernel where it applies (k % 128 == 0; K x packed-N
- * with n % 32 == 0), else the one-CTA kernel; route 1: the one-CTA kernel
+ * the register-fragment GEMV kernel for m <= 8 (K x packed-N with n % 16 ==
+ * 0, or N x packed-K), else the swap-AB kernel for m <= 8 (k % 128 == 0;
+ * K x packed-N with n % 32 == 0), else the CTA-pair kernel where it applies
+ * (k % 128 == 0; K x packed-N with n % 32 == 0), else the one-CTA kernel;
+ * route 1: the one-CTA kernel
  * for every shape; route 2: the CTA-pair kernel wherever it applies (never
  * a small-m one); route 3: the swap-AB kernel wherever it applies (m <=
  * 64); route 4: the register-fragment GEMV kernel wherever it applies

@@ -1,5 +1,5 @@
-"""The register-fragment W4A4 GEMV for at most 8 activation rows (route 4 of
-convrot_set_gemm_route): bitwise against the oracle's exact integer dot and
+"""The register-fragment W4A4 GEMV for at most 8 activation rows (the default
+kernel for m <= 8, pinned here by route 4 of convrot_set_gemm_route): bitwise against the oracle's exact integer dot and
 the reference epilogue order (core.py:932-936) on both weight layouts, every
 output dtype, m from 1 to 8, ragged n, K that is not a multiple of the
 kernel's K unit, K split over clusters of 1 to 8 CTAs and warps with empty K
@@ -117,3 +117,9 @@ def test_unsupported_shapes_fall_back():
     # call takes the tile kernels, still exact
     _check(3, 256, 40, _lib.LAYOUT_KN, torch.bfloat16, 9)
     assert _lib.load().convrot_set_gemm_route(5) == _lib.ERR_INVALID
+
+
+def test_default_route_takes_the_gemv():
+    _lib.check(_lib.load().convrot_set_gemm_route(0), "route")
+    _check(8, 3072, 1024, _lib.LAYOUT_KN, torch.bfloat16, 11)
+    _check(1, 1024, 200, _lib.LAYOUT_NK, torch.float16, 12)

@@ -280,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
   constexpr int SLOT = kKN ? kKnSlot : kNkSlot;
   constexpr int DEPTH = kKN ? kKnDepth : kNkDepth;
   static_assert(kWarps * kMaxRows * CB * 4 <= ring_bytes<LAYOUT>(), "partial sums overlay the rings");
+  static_assert(kThreads % CB == 0, "a thread's epilogue items share one column");
   // the warps' rings; after the K loop the same memory holds the per-warp
   // partial sums red[warp][row * CB + column]
   extern __shared__ __align__(128) uint8_t smem[];
@@ -310,12 +311,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
     if (i < units) issue_w(i);
     cp_async_commit();
   }
+  // The epilogue items of a thread (i = threadIdx.x + 256 j) share one
+  // column, i % CB == threadIdx.x % CB, so its weight scale and bias, which
+  // do not come from the previous kernel either, load now.
+  __shared__ float row_scale[kMaxRows];
+  const int my_n = n0 + static_cast<int>(threadIdx.x) % CB;
+  const float my_ws = (rank == 0 && my_n < p.N) ? __ldg(p.wscales + my_n) : 0.0f;
+  const float my_b = (rank == 0 && my_n < p.N && p.bias) ? __ldg(p.bias + my_n) : 0.0f;
   grid_dependency_wait();  // the activation codes may come from the previous kernel of the stream
   grid_dependents_launch();
 #pragma unroll
   for (int i = 0; i < DEPTH - 1; ++i)
     if (i < units) issue_a(i);
   cp_async_commit();
+  if (rank == 0 && threadIdx.x < p.M) row_scale[threadIdx.x] = __ldg(p.xscales + threadIdx.x);
 
   int32_t* mine = red + warp * kMaxRows * CB;
   // unit i and its activations have landed (this lane's copies): all but
@@ -402,10 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
         rem[q] = q < p.cluster ? dsmem_ld(mapa_shared(&red[i], static_cast<uint32_t>(q))) : 0u;
 #pragma unroll
       for (int q = 1; q < kMaxCluster; ++q) v += rem[q];
-      if (n < p.N) {
+      if (n < p.N) {  // n == my_n
         const int32_t dot = static_cast<int32_t>(v) >> 4;  // 16 * dot exactly
-        const float b = p.bias ? __ldg(p.bias + n) : 0.0f;
-        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(dot), __ldg(p.xscales + r)), __ldg(p.wscales + n)), b);
+        const float y = __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(dot), row_scale[r]), my_ws), my_b);
         out[static_cast<int64_t>(r) * p.N + n] = cvt_out<TOut>(y);
       }
     }

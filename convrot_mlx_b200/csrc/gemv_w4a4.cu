@@ -126,7 +126,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t a) {
 
 constexpr int kKnW = 32 * 64;           // weight bytes of a unit
 constexpr int kKnSlot = kKnW + 8 * 32;  // + 8 activation rows x 32 k
-constexpr int kKnDepth = 3;
+constexpr int kKnDepth = 4;
 
 struct KnStep {
   uint2 x[8];
@@ -330,9 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const Params p) {
   // unit i and its activations have landed (this lane's copies): all but
   // the min(i + 1, DEPTH - 1) most recent groups are complete
   auto wait_unit = [&](int i) {
-    static_assert(DEPTH >= 2 && DEPTH <= 4, "wait_unit covers rings of 2-4 units");
+    static_assert(DEPTH >= 2 && DEPTH <= 6, "wait_unit covers rings of 2-6 units");
     if (DEPTH >= 3 && i == 0) cp_async_wait<1>();
     else if (DEPTH >= 4 && i == 1) cp_async_wait<2>();
+    else if (DEPTH >= 5 && i == 2) cp_async_wait<3>();
+    else if (DEPTH >= 6 && i == 3) cp_async_wait<4>();
     else cp_async_wait<DEPTH - 1>();
   };
   auto refill = [&](int i) {

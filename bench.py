@@ -1009,9 +1009,10 @@ def run_video_tp(args, rank, world, local, steps: int, warmup: int):
 def run_case(args):
     """One kernel on one shape, launched ``--case-launches`` times on the
     default stream (eager), for profilers: ``--case gemm`` runs the W4A4 GEMM
-    (K x packed-N weights; the swap-AB kernel for m <= 8), ``--case prep``
+    (K x packed-N weights, on the kernel ``--route`` picks), ``--case prep``
     the fused rotate + A4 quantize, ``--case modnorm`` the same fused with a
-    modulated LayerNorm."""
+    modulated LayerNorm; ``--case dit`` runs that many eager denoise steps of
+    the W4A4 FLUX DiT (batch 8)."""
 
     import convrot_mlx_b200 as cr
     from convrot_mlx_b200 import _lib
@@ -1022,6 +1023,31 @@ def run_case(args):
     if args.case == "prep":
         for _ in range(args.case_launches):
             cr.metal_fused_prepare_convrot_activation_i8(x, args.group)
+    elif args.case == "dit":
+        # the W4A4 FLUX DiT of the dit entry (batch 8, one GPU, glue kernels and
+        # fused preps on): --case-launches eager denoise steps, the last inside
+        # an NVTX range "dit_step" (for ncu --nvtx-include "dit_step/")
+        import flux_dit
+        from convrot_mlx_b200.adapter import replace_convrot_linears
+
+        model = flux_dit.build_flux_dit(device, SEED)
+        flux_dit.build_glue()
+        model.fuse_attention_glue = True
+        replace_convrot_linears(model, backend="mpp-w4a4")
+        model.fuse_modulated_norm = True
+        img, txt, y, ids = flux_dit.dit_inputs(8, device, SEED + 7)
+        with torch.no_grad():
+            rope = model.rotary(ids)
+            t = torch.full((8,), 0.5, device=device)
+            guidance = torch.full((8,), 3.5, device=device)
+            for i in range(args.case_launches):
+                if i == args.case_launches - 1:
+                    torch.cuda.synchronize()
+                    torch.cuda.nvtx.range_push("dit_step")
+                v = model(img, txt, rope, t, y, guidance)
+                img.add_(-0.05 * v)
+            torch.cuda.nvtx.range_pop()
+        m, k, n = 8, 0, 0
     elif args.case == "modnorm":
         from convrot_mlx_b200.core import modulated_norm_prepare_i8
 
@@ -1085,7 +1111,7 @@ def main(argv=None):
                          "tensor-parallel and config-4 DiT entries added; flux-sweep: config 3 alone; video-tp: "
                          "config 5 alone; dit: config 4 alone; small-m: the m <= 64 GEMM entry alone")
     ap.add_argument("--dit-gens", type=int, default=2, help="timed 20-step generations per DiT arm in --workload all")
-    ap.add_argument("--case", choices=("gemm", "prep", "modnorm"), help="run one kernel on one shape (for profilers) and exit")
+    ap.add_argument("--case", choices=("gemm", "prep", "modnorm", "dit"), help="run one kernel on one shape (for profilers) and exit")
     ap.add_argument("--m", type=int, default=4096)
     ap.add_argument("--k", type=int, default=3072)
     ap.add_argument("--n", type=int, default=12288)

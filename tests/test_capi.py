@@ -76,6 +76,17 @@ def test_invalid_arguments_fail_before_any_device_work(lib):
     assert lib.convrot_unpack_int4(fake, 0, fake, None) == 0
 
 
+def test_gemm_route_range(lib):
+    # routes 0-4 (automatic, one-CTA, CTA-pair, swap-AB, GEMV) are accepted
+    # and touch no device; anything else is refused with a message
+    for route in (1, 2, 3, 4, 0):
+        assert lib.convrot_set_gemm_route(route) == 0
+    for route in (-1, 5):
+        assert lib.convrot_set_gemm_route(route) == -1
+        assert "0-4" in _err(lib)
+    assert lib.convrot_set_gemm_route(0) == 0
+
+
 def test_python_validation_matches_reference_messages():
     import convrot_mlx_b200 as cr
 
